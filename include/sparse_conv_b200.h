@@ -1,0 +1,172 @@
+/*
+ * sparse_conv_b200.h -- C ABI of the B200 (sm_100a) submanifold sparse conv3d
+ * engine (libsparseconv_b200.so).
+ *
+ * The library replaces the sparse-conv operator of TRELLIS.2:
+ *   - TS/WebGPU port: SparseConv3d.forward(x: SparseTensor, ctx)
+ *     (src/sparse/ops/conv3d.ts:41-222) with its three WGSL passes
+ *     (src/sparse/ops/conv3d_wgsl.ts:44-231);
+ *   - Python: the module selected by SPARSE_CONV_BACKEND under
+ *     trellis2/modules/sparse/conv (conv_none.py + hashmap_fallback.py,
+ *     README.md:27,109,111).
+ *
+ * Conventions (same operands as the reference):
+ *   coords   int32 [N,4] rows (b, x, y, z), device memory, 16-byte aligned,
+ *            0 <= b <= 32767, 0 <= x, y, z <= 65535
+ *            (src/sparse/sparse_tensor.ts:19)
+ *   feats    [N, Ci] row-major, dtype given per call
+ *   weight   [Co, Kd, Kh, Kw, Ci] row-major (checkpoint layout,
+ *            src/sparse/ops/conv3d.ts:5,19,48-49); 3x3x3 for submanifold,
+ *            2x2x2 for the stride-2 down/up convolutions
+ *   bias     [Co] in the feature dtype, or NULL (conv3d.ts:176-184)
+ *   out      [N_out, Co] in the feature dtype
+ * Kernel map: int32 [N_out, K]; column v = kd*9 + kh*3 + kw with kd on x,
+ * kh on y, kw on z (conv3d_wgsl.ts:91-101,115-117); value = input row of the
+ * neighbour with the same batch index, or -1 (absent / out of range).
+ *
+ * All pointers are caller-owned device pointers; the library never frees
+ * caller memory.  Calls enqueue work on the handle's stream and return; no C++
+ * exception crosses this boundary and nothing calls abort().  One handle per
+ * host thread.
+ */
+#ifndef SPARSE_CONV_B200_H
+#define SPARSE_CONV_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SC_API __attribute__((visibility("default")))
+#else
+#define SC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum sc_status {
+  SC_OK = 0,
+  SC_EINVAL = 1,        /* bad argument (null pointer, size, alignment, shape) */
+  SC_EDUP_COORD = 2,    /* two rows share (b, x, y, z) */
+  SC_ERANGE = 3,        /* b outside [0, 32767] or x, y, z outside [0, 65535] */
+  SC_ECUDA = 4,         /* CUDA runtime/driver error */
+  SC_ENCCL = 5,         /* collective error (sharded calls) */
+  SC_ETIMEOUT = 6,      /* a bounded device-side wait expired */
+  SC_ENOMEM = 7,        /* device allocation failed */
+  SC_EUNSUPPORTED = 8   /* valid request this build does not implement */
+} sc_status;
+
+typedef enum sc_dtype { SC_F32 = 0, SC_BF16 = 1, SC_F16 = 2 } sc_dtype;
+
+/* neighbour-map construction modes */
+enum { SC_MAP_HASH = 0, SC_MAP_SORT = 1 };
+/* kernel-map kinds */
+enum { SC_KMAP_SUBM = 0, SC_KMAP_DOWN2 = 1, SC_KMAP_UP2 = 2 };
+/* build flags */
+enum {
+  SC_BUILD_NO_TILE_SORT = 1u, /* keep output order for tiles (no mask sort) */
+  SC_BUILD_DEFER_CHECK = 2u   /* do not wait for the device error word */
+};
+/* conv epilogue flags, applied in this order: +bias, LayerNorm, SiLU, +residual */
+enum { SC_EPI_SILU = 1u, SC_EPI_RESIDUAL = 2u, SC_EPI_LAYERNORM = 4u };
+
+typedef struct sc_config {
+  int32_t device;       /* CUDA device ordinal */
+  int32_t map_mode;     /* SC_MAP_HASH (default) or SC_MAP_SORT */
+  int32_t debug_bounds; /* nonzero: check every gathered row index on device */
+  int32_t reserved;
+} sc_config;
+
+typedef struct sc_kmap_info {
+  int32_t kind;          /* SC_KMAP_* */
+  int32_t kernel_volume; /* K: 27 (3x3x3) or 8 (2x2x2) */
+  int64_t n_in;          /* rows of the input features */
+  int64_t n_out;         /* rows of the output */
+  int64_t num_pairs;     /* M: valid (output, offset) pairs */
+  int64_t num_tiles;     /* 128-row output tiles */
+  int64_t tile_pairs;    /* sum over tiles of 128 * popcount(tile offset mask) */
+} sc_kmap_info;
+
+typedef struct sc_handle sc_handle;
+typedef struct sc_kmap sc_kmap;
+
+/* Library version string. */
+SC_API const char* sc_version(void);
+
+/* Fills `cfg` with defaults (device 0, hash map mode, no debug checks). */
+SC_API void sc_config_default(sc_config* cfg);
+
+/* Per-device handle: owns the stream binding, memory pool settings and the
+ * last-error string.  Replaces the per-call GPUContext of the TS port
+ * (src/runtime/device.ts:30). */
+SC_API sc_status sc_create(sc_handle** out, const sc_config* cfg);
+SC_API sc_status sc_destroy(sc_handle* h);
+/* Enqueue all later work on `stream` (a cudaStream_t; NULL = legacy default). */
+SC_API sc_status sc_set_stream(sc_handle* h, void* stream);
+/* Waits for all work enqueued on the handle's stream. */
+SC_API sc_status sc_synchronize(sc_handle* h);
+/* Human-readable description of the last error on this handle. */
+SC_API const char* sc_last_error(const sc_handle* h);
+
+/* Submanifold neighbour map for a 3x3x3 kernel with dilation `dilation`.
+ * Replaces passes 0+1 (src/sparse/ops/conv3d.ts:73-151,
+ * conv3d_wgsl.ts:44-128) and hashmap_fallback.py (README.md:111).
+ * Unless SC_BUILD_DEFER_CHECK is set, waits for the build and returns
+ * SC_EDUP_COORD / SC_ERANGE for bad coordinates. */
+SC_API sc_status sc_kmap_build(sc_handle* h, const int32_t* coords, int64_t n, int32_t kernel_size, int32_t dilation,
+                        uint32_t flags, sc_kmap** out);
+
+/* Stride-2 2x2x2 down-sample map: parents are the unique (b, x>>1, y>>1, z>>1)
+ * in ascending lexicographic order; map column = (x&1)*4 + (y&1)*2 + (z&1).
+ * Replaces the stride-2 sparse conv of trellis2/modules/sparse/conv (absent
+ * from the reference tree; semantics fixed by this ABI).  Waits for the
+ * parent count. */
+SC_API sc_status sc_kmap_build_down2(sc_handle* h, const int32_t* coords, int64_t n, uint32_t flags, sc_kmap** out);
+
+/* Transposed 2x2x2 map from a down-sample map: outputs are the fine rows,
+ * inputs the parents; row c uses column slot(c) and reads parent(c). */
+SC_API sc_status sc_kmap_build_up2(sc_handle* h, const sc_kmap* down, uint32_t flags, sc_kmap** out);
+
+/* Parent coords of a down-sample map: int32 [n_out, 4]. */
+SC_API sc_status sc_kmap_out_coords(sc_handle* h, const sc_kmap* km, int32_t* coords_out);
+
+/* Writes the canonical int32 [n_out, K] map (for bit-exact checks). */
+SC_API sc_status sc_kmap_export(sc_handle* h, const sc_kmap* km, int32_t* map_out);
+
+/* Sizes and pair counts (waits for the build to finish). */
+SC_API sc_status sc_kmap_get_info(sc_handle* h, const sc_kmap* km, sc_kmap_info* info);
+
+/* Waits for the build and returns its device-side status. */
+SC_API sc_status sc_kmap_check(sc_handle* h, const sc_kmap* km);
+
+SC_API sc_status sc_kmap_free(sc_handle* h, sc_kmap* km);
+
+/* out[n] = epilogue(bias + sum_v W[:, v, :] . feats[map[n, v]]).
+ * Replaces pass 2 (src/sparse/ops/conv3d.ts:154-221, conv3d_wgsl.ts:132-231)
+ * and conv_none.py (README.md:109).  bf16/f16: tcgen05 tensor cores with f32
+ * accumulation; f32: f32 FMA.  `residual` is [n_out, Co] (SC_EPI_RESIDUAL),
+ * LayerNorm has no affine and uses `ln_eps`. */
+SC_API sc_status sc_conv3d(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight, const void* bias,
+                    const void* residual, void* out, int32_t ci, int32_t co, sc_dtype dtype, uint32_t epilogue,
+                    float ln_eps);
+
+/* Named entry points for the three operator kinds; each checks the map kind
+ * and forwards to sc_conv3d. */
+SC_API sc_status sc_conv3d_subm(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight, const void* bias,
+                         const void* residual, void* out, int32_t ci, int32_t co, sc_dtype dtype, uint32_t epilogue,
+                         float ln_eps);
+SC_API sc_status sc_conv3d_down2(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight,
+                          const void* bias, void* out, int32_t ci, int32_t co, sc_dtype dtype, uint32_t epilogue);
+SC_API sc_status sc_conv3d_up2(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight, const void* bias,
+                        void* out, int32_t ci, int32_t co, sc_dtype dtype, uint32_t epilogue);
+
+/* Row LayerNorm (no affine) + optional SiLU, in place on [n, c] features
+ * (src/dense/ops/layer_norm.ts:28-60, src/dense/ops/silu.ts:20-31). */
+SC_API sc_status sc_layernorm_silu(sc_handle* h, void* x, int64_t n, int32_t c, sc_dtype dtype, int32_t apply_silu,
+                            float eps);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARSE_CONV_B200_H */

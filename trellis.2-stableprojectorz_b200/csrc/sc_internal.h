@@ -1,0 +1,77 @@
+// Internal structures shared by the engine's translation units.
+#pragma once
+#include <cstdint>
+#include <string>
+#include <cuda_runtime.h>
+#include "../../include/sparse_conv_b200.h"
+
+namespace sc {
+
+// Output rows are processed in tiles of this many rows (one TMEM lane each).
+constexpr int kTileRows = 128;
+
+struct Handle {
+  int device = 0;
+  int map_mode = SC_MAP_HASH;
+  int debug_bounds = 0;
+  cudaStream_t stream = nullptr;
+  int num_sms = 148;
+  int* derr = nullptr;  // device error word written by conv kernels
+  std::string last_error;
+};
+
+// Neighbour / gather map in the layout the conv kernels consume.
+//
+//   tile_rows[t*128 + i]      output row handled by slot i of tile t (-1 = pad)
+//   tile_mask[t]              bit v set when some row of tile t has offset v
+//   gidx[(t*K + v)*128 + i]   input row gathered for slot i, offset v (-1 = none)
+//
+// Tiles are formed after sorting output rows by their K-bit neighbour mask
+// (stable), so rows of one tile share most of their offsets.
+struct KMap {
+  int kind = SC_KMAP_SUBM;
+  int K = 27;
+  int64_t n_in = 0;
+  int64_t n_out = 0;
+  int64_t num_tiles = 0;
+  int32_t* gidx = nullptr;
+  int32_t* tile_rows = nullptr;
+  uint32_t* tile_mask = nullptr;
+  int32_t* out_coords = nullptr;   // down-sample: parent coords [n_out, 4]
+  int32_t* parent_of = nullptr;    // down-sample: parent of every fine row [n_in]
+  unsigned long long* counters = nullptr;  // [0] valid pairs, [1] tile pairs
+  int* err = nullptr;              // device error word of the build
+};
+
+// Helpers implemented in sc_api.cu
+cudaError_t dev_alloc(Handle* h, void** p, size_t bytes);
+void dev_free(Handle* h, void* p);
+
+// kmap construction (sc_kmap.cu)
+sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int dilation, uint32_t flags, KMap** out);
+sc_status build_down2(Handle* h, const int32_t* coords, int64_t n, uint32_t flags, KMap** out);
+sc_status build_up2(Handle* h, const KMap* down, uint32_t flags, KMap** out);
+sc_status export_map(Handle* h, const KMap* km, int32_t* map_out);
+void free_kmap(Handle* h, KMap* km);
+
+// conv launchers
+sc_status conv_tc(Handle* h, const KMap* km, const void* feats, const void* weight, const void* bias,
+                  const void* residual, void* out, int ci, int co, sc_dtype dtype, uint32_t epi, float eps);
+sc_status conv_simt_f32(Handle* h, const KMap* km, const float* feats, const float* weight, const float* bias,
+                        const float* residual, float* out, int ci, int co, uint32_t epi, float eps);
+sc_status check_gather_bounds(Handle* h, const KMap* km);
+sc_status layernorm_silu(Handle* h, void* x, int64_t n, int c, sc_dtype dtype, int silu, float eps);
+
+// radix sort (sc_sort.cu): sorts (key, value) pairs on bits [begin_bit, end_bit)
+size_t radix_sort_temp_bytes(int64_t n, int key_bytes, int passes);
+sc_status radix_sort_pairs_u64(Handle* h, uint64_t* keys, uint32_t* vals, uint64_t* keys_alt, uint32_t* vals_alt,
+                               int64_t n, int begin_bit, int end_bit, void* temp, size_t temp_bytes, int* err,
+                               bool* result_in_alt);
+sc_status radix_sort_pairs_u32(Handle* h, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,
+                               int64_t n, int begin_bit, int end_bit, void* temp, size_t temp_bytes, int* err,
+                               bool* result_in_alt);
+
+sc_status set_error(Handle* h, sc_status st, const std::string& msg);
+sc_status cuda_error(Handle* h, cudaError_t e, const char* what);
+
+}  // namespace sc

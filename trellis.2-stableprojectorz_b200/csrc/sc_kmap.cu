@@ -1,0 +1,735 @@
+// Kernel-map construction: submanifold 3x3x3 (hash or sort probe), stride-2
+// down-sample and its transpose, then the tile layout the conv kernels read.
+//
+// Reference behaviour being replaced:
+//   pass 0  src/sparse/ops/conv3d_wgsl.ts:44-71   dense sp_to_lin scatter
+//   pass 1  src/sparse/ops/conv3d_wgsl.ts:75-128  27-offset neighbour lookup
+//   host    src/sparse/ops/conv3d.ts:63-151        cache + dispatch
+//   hashmap_fallback.py (README.md:111)            flat_idx sort + searchsorted
+// The dense grid is replaced by an open-addressing hash (or a sorted key
+// array); the batch index is part of every key.
+#include "sc_common.cuh"
+#include "sc_internal.h"
+
+#include <algorithm>
+#include <vector>
+
+namespace sc {
+namespace {
+
+constexpr unsigned long long kEmptyKey = ~0ull;
+
+struct __align__(16) Slot {
+  unsigned long long key;
+  int val;
+  int pad;
+};
+
+// 16-bit fields: b | x | y | z (b <= 32767, x/y/z <= 65535, checked).
+__device__ __forceinline__ unsigned long long pack16(int b, int x, int y, int z) {
+  return (static_cast<unsigned long long>(b) << 48) | (static_cast<unsigned long long>(x) << 32) |
+         (static_cast<unsigned long long>(y) << 16) | static_cast<unsigned long long>(z);
+}
+
+// 64-bit mixing finaliser (MurmurHash3 fmix64), folded to 32 bits.
+__device__ __forceinline__ uint32_t mix64(unsigned long long k) {
+  k ^= k >> 33;
+  k *= 0xff51afd7ed558ccdull;
+  k ^= k >> 33;
+  k *= 0xc4ceb9fe1a85ec53ull;
+  k ^= k >> 33;
+  return static_cast<uint32_t>(k);
+}
+
+// Batch index in [0, 32767] keeps the top key bit clear, so the all-ones
+// empty-slot key can never collide with a voxel key.
+__device__ __forceinline__ bool coord_ok(int4 c) {
+  return static_cast<unsigned>(c.x) <= 32767u && static_cast<unsigned>(c.y) <= 65535u &&
+         static_cast<unsigned>(c.z) <= 65535u && static_cast<unsigned>(c.w) <= 65535u;
+}
+
+__device__ __forceinline__ void offset27(int v, int dil, int& dx, int& dy, int& dz) {
+  dx = (v / 9 - 1) * dil;
+  dy = ((v / 3) % 3 - 1) * dil;
+  dz = (v % 3 - 1) * dil;
+}
+
+__global__ void k_iota(uint32_t* v, int64_t n) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i < n) v[i] = static_cast<uint32_t>(i);
+}
+
+__global__ void k_hash_insert(const int4* __restrict__ coords, int64_t n, Slot* slots, uint32_t cap_mask, int* err) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i >= n) return;
+  const int4 c = coords[i];
+  if (!coord_ok(c)) {
+    record_error(err, SC_ERANGE);
+    return;
+  }
+  const unsigned long long key = pack16(c.x, c.y, c.z, c.w);
+  uint32_t hpos = mix64(key) & cap_mask;
+  for (uint32_t it = 0; it <= cap_mask; ++it) {
+    const unsigned long long prev = atomicCAS(&slots[hpos].key, kEmptyKey, key);
+    if (prev == kEmptyKey) {
+      slots[hpos].val = static_cast<int>(i);
+      return;
+    }
+    if (prev == key) {
+      record_error(err, SC_EDUP_COORD);
+      return;
+    }
+    hpos = (hpos + 1) & cap_mask;
+  }
+  record_error(err, SC_ENOMEM);
+}
+
+__device__ __forceinline__ int hash_find(const Slot* __restrict__ slots, uint32_t cap_mask, unsigned long long key,
+                                         uint32_t hpos, unsigned long long k0, int v0) {
+  if (k0 == key) return v0;
+  if (k0 == kEmptyKey) return -1;
+  for (uint32_t it = 0; it < cap_mask; ++it) {
+    hpos = (hpos + 1) & cap_mask;
+    const ulonglong2 s = __ldg(reinterpret_cast<const ulonglong2*>(slots) + hpos);
+    if (s.x == key) return static_cast<int>(static_cast<uint32_t>(s.y));
+    if (s.x == kEmptyKey) return -1;
+  }
+  return -1;
+}
+
+__device__ __forceinline__ void write_rows_and_count(const int32_t* s_map, int64_t row0, int64_t n, int K,
+                                                     int32_t* __restrict__ map, uint32_t m,
+                                                     unsigned long long* counters) {
+  __syncthreads();
+  const int rows = static_cast<int>(min(static_cast<int64_t>(blockDim.x), n - row0));
+  const int total = rows * K;
+  for (int j = threadIdx.x; j < total; j += blockDim.x) map[row0 * K + j] = s_map[j];
+  unsigned cnt = __popc(m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  if ((threadIdx.x & 31) == 0 && cnt) atomicAdd(&counters[0], static_cast<unsigned long long>(cnt));
+}
+
+// One thread per output voxel: 27 hash probes (centre = self), row staged in
+// shared memory so the [N,27] map is written with coalesced stores.
+__global__ void __launch_bounds__(128) k_probe_hash(const int4* __restrict__ coords, int64_t n,
+                                                    const Slot* __restrict__ slots, uint32_t cap_mask, int dil,
+                                                    int32_t* __restrict__ map, uint32_t* __restrict__ row_mask,
+                                                    unsigned long long* counters) {
+  __shared__ int32_t s_map[128 * 27];
+  const int64_t row0 = blockIdx.x * 128ll;
+  const int64_t i = row0 + threadIdx.x;
+  uint32_t m = 0;
+  if (i < n) {
+    const int4 c = coords[i];
+    unsigned long long q[27];
+    uint32_t hp[27];
+    ulonglong2 s0[27];
+#pragma unroll
+    for (int v = 0; v < 27; ++v) {
+      int dx, dy, dz;
+      offset27(v, dil, dx, dy, dz);
+      const int x = c.y + dx, y = c.z + dy, z = c.w + dz;
+      const bool inb = static_cast<unsigned>(x) <= 65535u && static_cast<unsigned>(y) <= 65535u &&
+                       static_cast<unsigned>(z) <= 65535u && coord_ok(c);
+      q[v] = inb ? pack16(c.x, x, y, z) : kEmptyKey;
+      hp[v] = mix64(q[v]) & cap_mask;
+      s0[v] = (v != 13 && inb) ? __ldg(reinterpret_cast<const ulonglong2*>(slots) + hp[v]) : make_ulonglong2(0, 0);
+    }
+#pragma unroll
+    for (int v = 0; v < 27; ++v) {
+      int r;
+      if (v == 13) {
+        r = static_cast<int>(i);
+      } else if (q[v] == kEmptyKey) {
+        r = -1;
+      } else {
+        r = hash_find(slots, cap_mask, q[v], hp[v], s0[v].x, static_cast<int>(static_cast<uint32_t>(s0[v].y)));
+      }
+      s_map[threadIdx.x * 27 + v] = r;
+      m |= (r >= 0 ? 1u : 0u) << v;
+    }
+    row_mask[i] = m;
+  }
+  write_rows_and_count(s_map, row0, n, 27, map, m, counters);
+}
+
+// ---------------------------------------------------------------- sort mode
+struct Packing {
+  int wx, wy, wz;     // bit widths of x, y, z fields
+  int mx, my, mz;     // maxima (neighbours beyond them do not exist)
+};
+
+__device__ __forceinline__ unsigned long long pack_compact(int b, int x, int y, int z, const Packing& pk) {
+  return (((static_cast<unsigned long long>(b) << pk.wx | static_cast<unsigned long long>(x)) << pk.wy |
+           static_cast<unsigned long long>(y))
+          << pk.wz) |
+         static_cast<unsigned long long>(z);
+}
+
+__global__ void k_minmax(const int4* __restrict__ coords, int64_t n, int shift, int* maxes, int* err) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  int4 c = make_int4(0, 0, 0, 0);
+  if (i < n) {
+    c = coords[i];
+    if (!coord_ok(c)) {
+      record_error(err, SC_ERANGE);
+      c = make_int4(0, 0, 0, 0);
+    }
+  }
+  int mb = c.x, mx = c.y >> shift, my = c.z >> shift, mz = c.w >> shift;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    my = max(my, __shfl_xor_sync(0xffffffffu, my, o));
+    mz = max(mz, __shfl_xor_sync(0xffffffffu, mz, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(&maxes[0], mb);
+    atomicMax(&maxes[1], mx);
+    atomicMax(&maxes[2], my);
+    atomicMax(&maxes[3], mz);
+  }
+}
+
+__global__ void k_pack_keys(const int4* __restrict__ coords, int64_t n, int shift, Packing pk,
+                            unsigned long long* keys, uint32_t* vals) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i >= n) return;
+  int4 c = coords[i];
+  if (!coord_ok(c)) c = make_int4(0, 0, 0, 0);  // error already recorded by k_minmax
+  keys[i] = pack_compact(c.x, c.y >> shift, c.z >> shift, c.w >> shift, pk);
+  vals[i] = static_cast<uint32_t>(i);
+}
+
+__global__ void k_check_sorted_unique(const unsigned long long* __restrict__ skeys, int64_t n, int* err) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i >= 1 && i < n && skeys[i] == skeys[i - 1]) record_error(err, SC_EDUP_COORD);
+}
+
+__device__ __forceinline__ int sorted_find(const unsigned long long* __restrict__ skeys,
+                                           const uint32_t* __restrict__ svals, int64_t n, unsigned long long q) {
+  int64_t lo = 0, hi = n;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (__ldg(skeys + mid) < q) lo = mid + 1; else hi = mid;
+  }
+  return (lo < n && __ldg(skeys + lo) == q) ? static_cast<int>(__ldg(svals + lo)) : -1;
+}
+
+__global__ void __launch_bounds__(128) k_probe_sorted(const int4* __restrict__ coords, int64_t n,
+                                                      const unsigned long long* __restrict__ skeys,
+                                                      const uint32_t* __restrict__ svals, Packing pk, int dil,
+                                                      int32_t* __restrict__ map, uint32_t* __restrict__ row_mask,
+                                                      unsigned long long* counters) {
+  __shared__ int32_t s_map[128 * 27];
+  const int64_t row0 = blockIdx.x * 128ll;
+  const int64_t i = row0 + threadIdx.x;
+  uint32_t m = 0;
+  if (i < n) {
+    int4 c = coords[i];
+    const bool cok = coord_ok(c);
+#pragma unroll 1
+    for (int v = 0; v < 27; ++v) {
+      int dx, dy, dz;
+      offset27(v, dil, dx, dy, dz);
+      const int x = c.y + dx, y = c.z + dy, z = c.w + dz;
+      int r = -1;
+      if (v == 13) {
+        r = static_cast<int>(i);
+      } else if (cok && x >= 0 && y >= 0 && z >= 0 && x <= pk.mx && y <= pk.my && z <= pk.mz) {
+        r = sorted_find(skeys, svals, n, pack_compact(c.x, x, y, z, pk));
+      }
+      s_map[threadIdx.x * 27 + v] = r;
+      m |= (r >= 0 ? 1u : 0u) << v;
+    }
+    row_mask[i] = m;
+  }
+  write_rows_and_count(s_map, row0, n, 27, map, m, counters);
+}
+
+// --------------------------------------------------------- down / up maps
+// Scan helpers (3 kernels, no inter-block waits): parent id of every sorted entry.
+constexpr int kScanBlock = 1024;
+
+__global__ void k_heads_count(const unsigned long long* __restrict__ skeys, int64_t n, uint32_t* block_sums) {
+  __shared__ uint32_t s[32];
+  const int64_t i0 = blockIdx.x * static_cast<int64_t>(kScanBlock);
+  uint32_t c = 0;
+  for (int j = threadIdx.x; j < kScanBlock; j += blockDim.x) {
+    const int64_t i = i0 + j;
+    if (i < n && (i == 0 || skeys[i] != skeys[i - 1])) ++c;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t t = 0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += s[w];
+    block_sums[blockIdx.x] = t;
+  }
+}
+
+__global__ void k_scan_block_sums(uint32_t* block_sums, int64_t nb, uint32_t* total) {
+  // single block of 1024 threads; exclusive scan in place, in chunks
+  __shared__ uint32_t s[1024];
+  uint32_t carry = 0;
+  for (int64_t base = 0; base < nb; base += 1024) {
+    const int64_t i = base + threadIdx.x;
+    const uint32_t x = i < nb ? block_sums[i] : 0u;
+    s[threadIdx.x] = x;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {
+      const uint32_t y = threadIdx.x >= static_cast<unsigned>(o) ? s[threadIdx.x - o] : 0u;
+      __syncthreads();
+      s[threadIdx.x] += y;
+      __syncthreads();
+    }
+    if (i < nb) block_sums[i] = carry + s[threadIdx.x] - x;
+    const uint32_t chunk_total = s[1023];
+    __syncthreads();
+    carry += chunk_total;
+  }
+  if (threadIdx.x == 0) *total = carry;
+}
+
+__global__ void k_heads_assign(const unsigned long long* __restrict__ skeys, int64_t n,
+                               const uint32_t* __restrict__ block_sums, uint32_t* __restrict__ pid) {
+  // 1024 threads per block, one element each
+  __shared__ uint32_t s[1024];
+  const int64_t i = blockIdx.x * static_cast<int64_t>(kScanBlock) + threadIdx.x;
+  const uint32_t f = (i < n && (i == 0 || skeys[i] != skeys[i - 1])) ? 1u : 0u;
+  s[threadIdx.x] = f;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {
+    const uint32_t y = threadIdx.x >= static_cast<unsigned>(o) ? s[threadIdx.x - o] : 0u;
+    __syncthreads();
+    s[threadIdx.x] += y;
+    __syncthreads();
+  }
+  if (i < n) pid[i] = block_sums[blockIdx.x] + s[threadIdx.x] - 1u;
+}
+
+__global__ void k_down_fill(const unsigned long long* __restrict__ skeys, const uint32_t* __restrict__ svals,
+                            const uint32_t* __restrict__ pid, const int4* __restrict__ coords, int64_t n,
+                            int32_t* dmap, int32_t* out_coords, int32_t* parent_code, int* err) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t c = svals[i];
+  const uint32_t p = pid[i];
+  const int4 cc = coords[c];
+  const int slot = (cc.y & 1) * 4 + (cc.z & 1) * 2 + (cc.w & 1);
+  const int prev = atomicExch(&dmap[static_cast<int64_t>(p) * 8 + slot], static_cast<int>(c));
+  if (prev != -1) record_error(err, SC_EDUP_COORD);
+  parent_code[c] = static_cast<int32_t>(p * 8u + static_cast<uint32_t>(slot));
+  if (i == 0 || skeys[i] != skeys[i - 1]) {
+    reinterpret_cast<int4*>(out_coords)[p] = make_int4(cc.x, cc.y >> 1, cc.z >> 1, cc.w >> 1);
+  }
+}
+
+__global__ void k_row_masks(const int32_t* __restrict__ map, int64_t n, int K, uint32_t* row_mask,
+                            unsigned long long* counters) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  uint32_t m = 0;
+  if (i < n) {
+    for (int v = 0; v < K; ++v) m |= (map[i * K + v] >= 0 ? 1u : 0u) << v;
+    row_mask[i] = m;
+  }
+  unsigned cnt = __popc(m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  if ((threadIdx.x & 31) == 0 && cnt) atomicAdd(&counters[0], static_cast<unsigned long long>(cnt));
+}
+
+__global__ void k_up_fill(const int32_t* __restrict__ parent_code, int64_t n, int32_t* umap, uint32_t* row_mask) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i >= n) return;
+  const int32_t code = parent_code[i];
+  const int slot = code & 7;
+  umap[i * 8 + slot] = code >> 3;
+  row_mask[i] = 1u << slot;
+}
+
+// ------------------------------------------------------------- tile layout
+__global__ void __launch_bounds__(128) k_build_tiles(const int32_t* __restrict__ map, int K,
+                                                     const uint32_t* __restrict__ perm, int64_t n_out,
+                                                     const uint32_t* __restrict__ row_mask, int32_t* gidx,
+                                                     int32_t* tile_rows, uint32_t* tile_mask,
+                                                     unsigned long long* counters) {
+  __shared__ uint32_t s_or[4];
+  const int64_t t = blockIdx.x;
+  const int i = threadIdx.x;
+  const int64_t s = t * kTileRows + i;
+  const int r = s < n_out ? static_cast<int>(perm[s]) : -1;
+  tile_rows[s] = r;
+  uint32_t m = r >= 0 ? row_mask[r] : 0u;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m |= __shfl_xor_sync(0xffffffffu, m, o);
+  if ((i & 31) == 0) s_or[i >> 5] = m;
+  for (int v = 0; v < K; ++v) {
+    gidx[(t * K + v) * kTileRows + i] = r >= 0 ? __ldg(map + static_cast<int64_t>(r) * K + v) : -1;
+  }
+  __syncthreads();
+  if (i == 0) {
+    const uint32_t tm = s_or[0] | s_or[1] | s_or[2] | s_or[3];
+    tile_mask[t] = tm;
+    atomicAdd(&counters[1], static_cast<unsigned long long>(kTileRows) * __popc(tm));
+  }
+}
+
+__global__ void k_export(const int32_t* __restrict__ gidx, const int32_t* __restrict__ tile_rows, int64_t num_tiles,
+                         int K, int32_t* __restrict__ map_out) {
+  const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (e >= num_tiles * K * kTileRows) return;
+  const int i = static_cast<int>(e % kTileRows);
+  const int64_t tv = e / kTileRows;
+  const int64_t t = tv / K;
+  const int v = static_cast<int>(tv % K);
+  const int r = tile_rows[t * kTileRows + i];
+  if (r >= 0) map_out[static_cast<int64_t>(r) * K + v] = gidx[e];
+}
+
+inline unsigned blocks_for(int64_t n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
+
+int bit_width(int v) {
+  int w = 0;
+  while (w < 31 && (v >> w) != 0) ++w;
+  return w;
+}
+
+// RAII list of stream-ordered temporaries.
+struct Temps {
+  Handle* h;
+  std::vector<void*> ptrs;
+  explicit Temps(Handle* hh) : h(hh) {}
+  ~Temps() {
+    for (void* p : ptrs) dev_free(h, p);
+  }
+  template <typename T>
+  cudaError_t get(T** p, size_t bytes) {
+    void* q = nullptr;
+    cudaError_t e = dev_alloc(h, &q, bytes ? bytes : 16);
+    if (e == cudaSuccess) ptrs.push_back(q);
+    *p = static_cast<T*>(q);
+    return e;
+  }
+};
+
+#define SC_TRY_CUDA(expr, what)                 \
+  do {                                          \
+    cudaError_t _e = (expr);                    \
+    if (_e != cudaSuccess) return cuda_error(h, _e, what); \
+  } while (0)
+
+// Allocates the persistent parts of a map (owned by the KMap).
+sc_status alloc_kmap(Handle* h, KMap* km) {
+  km->num_tiles = (km->n_out + kTileRows - 1) / kTileRows;
+  const int64_t slots = std::max<int64_t>(km->num_tiles, 1) * kTileRows;
+  SC_TRY_CUDA(dev_alloc(h, reinterpret_cast<void**>(&km->gidx), sizeof(int32_t) * slots * km->K), "alloc gidx");
+  SC_TRY_CUDA(dev_alloc(h, reinterpret_cast<void**>(&km->tile_rows), sizeof(int32_t) * slots), "alloc tile_rows");
+  SC_TRY_CUDA(dev_alloc(h, reinterpret_cast<void**>(&km->tile_mask),
+                        sizeof(uint32_t) * std::max<int64_t>(km->num_tiles, 1)),
+              "alloc tile_mask");
+  return SC_OK;
+}
+
+// Orders output rows by neighbour mask and writes gidx / tile_rows / tile_mask.
+sc_status finish_tiles(Handle* h, KMap* km, const int32_t* map, uint32_t* row_mask, uint32_t flags, Temps& tmp) {
+  const int64_t n = km->n_out;
+  if (n == 0) return SC_OK;
+  uint32_t *perm, *perm_alt, *mask_alt, *mask_copy;
+  SC_TRY_CUDA(tmp.get(&perm, sizeof(uint32_t) * n), "alloc perm");
+  k_iota<<<blocks_for(n, 256), 256, 0, h->stream>>>(perm, n);
+  const uint32_t* order = perm;
+  if (!(flags & SC_BUILD_NO_TILE_SORT)) {
+    SC_TRY_CUDA(tmp.get(&perm_alt, sizeof(uint32_t) * n), "alloc perm");
+    SC_TRY_CUDA(tmp.get(&mask_alt, sizeof(uint32_t) * n), "alloc masks");
+    SC_TRY_CUDA(tmp.get(&mask_copy, sizeof(uint32_t) * n), "alloc masks");
+    SC_TRY_CUDA(cudaMemcpyAsync(mask_copy, row_mask, sizeof(uint32_t) * n, cudaMemcpyDeviceToDevice, h->stream),
+                "copy masks");
+    const int passes = (km->K + 7) / 8;
+    const size_t tb = radix_sort_temp_bytes(n, 4, passes);
+    void* temp;
+    SC_TRY_CUDA(tmp.get(&temp, tb), "alloc sort temp");
+    bool in_alt = false;
+    sc_status st = radix_sort_pairs_u32(h, mask_copy, perm, mask_alt, perm_alt, n, 0, km->K, temp, tb, km->err,
+                                        &in_alt);
+    if (st != SC_OK) return st;
+    order = in_alt ? perm_alt : perm;
+  }
+  k_build_tiles<<<static_cast<unsigned>(km->num_tiles), kTileRows, 0, h->stream>>>(
+      map, km->K, order, n, row_mask, km->gidx, km->tile_rows, km->tile_mask, km->counters);
+  SC_TRY_CUDA(cudaGetLastError(), "tile build launch");
+  return SC_OK;
+}
+
+sc_status new_kmap(Handle* h, int kind, int K, int64_t n_in, int64_t n_out, KMap** out) {
+  KMap* km = new (std::nothrow) KMap();
+  if (!km) return set_error(h, SC_ENOMEM, "host allocation failed");
+  km->kind = kind;
+  km->K = K;
+  km->n_in = n_in;
+  km->n_out = n_out;
+  cudaError_t e = dev_alloc(h, reinterpret_cast<void**>(&km->counters), 64);
+  if (e == cudaSuccess) e = cudaMemsetAsync(km->counters, 0, 64, h->stream);
+  if (e != cudaSuccess) {
+    free_kmap(h, km);
+    return cuda_error(h, e, "alloc kmap counters");
+  }
+  km->err = reinterpret_cast<int*>(km->counters + 4);
+  *out = km;
+  return SC_OK;
+}
+
+// Reads the device maxima of (b, x>>shift, y>>shift, z>>shift); synchronises.
+sc_status read_maxima(Handle* h, const int32_t* coords, int64_t n, int shift, int* err, Temps& tmp, int hmax[4]) {
+  int* dmax;
+  SC_TRY_CUDA(tmp.get(&dmax, 16), "alloc maxima");
+  SC_TRY_CUDA(cudaMemsetAsync(dmax, 0, 16, h->stream), "memset maxima");
+  k_minmax<<<blocks_for(n, 256), 256, 0, h->stream>>>(reinterpret_cast<const int4*>(coords), n, shift, dmax, err);
+  int herr = 0;
+  SC_TRY_CUDA(cudaMemcpyAsync(hmax, dmax, 16, cudaMemcpyDeviceToHost, h->stream), "copy maxima");
+  SC_TRY_CUDA(cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, h->stream), "copy err");
+  SC_TRY_CUDA(cudaStreamSynchronize(h->stream), "sync maxima");
+  if (herr == SC_ERANGE) return set_error(h, SC_ERANGE, "coordinate out of range (b in [0, 32767], x/y/z in [0, 65535])");
+  return SC_OK;
+}
+
+}  // namespace
+
+sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int dilation, uint32_t flags, KMap** out) {
+  KMap* km = nullptr;
+  sc_status st = new_kmap(h, SC_KMAP_SUBM, 27, n, n, &km);
+  if (st != SC_OK) return st;
+  Temps tmp(h);
+  st = alloc_kmap(h, km);
+  if (st != SC_OK || n == 0) {
+    if (st != SC_OK) free_kmap(h, km); else *out = km;
+    return st;
+  }
+  int32_t* map;
+  uint32_t* row_mask;
+  cudaError_t e = tmp.get(&map, sizeof(int32_t) * n * 27);
+  if (e == cudaSuccess) e = tmp.get(&row_mask, sizeof(uint32_t) * n);
+  if (e != cudaSuccess) {
+    free_kmap(h, km);
+    return cuda_error(h, e, "alloc map");
+  }
+  const int4* c4 = reinterpret_cast<const int4*>(coords);
+  if (h->map_mode == SC_MAP_SORT) {
+    int hmax[4];
+    st = read_maxima(h, coords, n, 0, km->err, tmp, hmax);
+    if (st != SC_OK) {
+      free_kmap(h, km);
+      return st;
+    }
+    Packing pk{bit_width(hmax[1]), bit_width(hmax[2]), bit_width(hmax[3]), hmax[1], hmax[2], hmax[3]};
+    const int bits = bit_width(hmax[0]) + pk.wx + pk.wy + pk.wz;
+    unsigned long long *keys, *keys_alt;
+    uint32_t *vals, *vals_alt;
+    void* temp;
+    const int passes = std::max(1, (bits + 7) / 8);
+    const size_t tb = radix_sort_temp_bytes(n, 8, passes);
+    e = tmp.get(&keys, 8 * n);
+    if (e == cudaSuccess) e = tmp.get(&keys_alt, 8 * n);
+    if (e == cudaSuccess) e = tmp.get(&vals, 4 * n);
+    if (e == cudaSuccess) e = tmp.get(&vals_alt, 4 * n);
+    if (e == cudaSuccess) e = tmp.get(&temp, tb);
+    if (e != cudaSuccess) {
+      free_kmap(h, km);
+      return cuda_error(h, e, "alloc sort buffers");
+    }
+    k_pack_keys<<<blocks_for(n, 256), 256, 0, h->stream>>>(c4, n, 0, pk, keys, vals);
+    bool in_alt = false;
+    st = radix_sort_pairs_u64(h, reinterpret_cast<uint64_t*>(keys), vals, reinterpret_cast<uint64_t*>(keys_alt),
+                              vals_alt, n, 0, std::max(bits, 1), temp, tb, km->err, &in_alt);
+    if (st != SC_OK) {
+      free_kmap(h, km);
+      return st;
+    }
+    const unsigned long long* sk = in_alt ? keys_alt : keys;
+    const uint32_t* sv = in_alt ? vals_alt : vals;
+    k_check_sorted_unique<<<blocks_for(n, 256), 256, 0, h->stream>>>(sk, n, km->err);
+    k_probe_sorted<<<blocks_for(n, 128), 128, 0, h->stream>>>(c4, n, sk, sv, pk, dilation, map, row_mask,
+                                                               km->counters);
+  } else {
+    uint32_t cap = 1024;
+    while (cap < 2 * n) cap <<= 1;
+    Slot* slots;
+    e = tmp.get(&slots, sizeof(Slot) * cap);
+    if (e == cudaSuccess) e = cudaMemsetAsync(slots, 0xFF, sizeof(Slot) * cap, h->stream);
+    if (e != cudaSuccess) {
+      free_kmap(h, km);
+      return cuda_error(h, e, "alloc hash table");
+    }
+    k_hash_insert<<<blocks_for(n, 256), 256, 0, h->stream>>>(c4, n, slots, cap - 1, km->err);
+    k_probe_hash<<<blocks_for(n, 128), 128, 0, h->stream>>>(c4, n, slots, cap - 1, dilation, map, row_mask,
+                                                             km->counters);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    free_kmap(h, km);
+    return cuda_error(h, e, "map build launch");
+  }
+  st = finish_tiles(h, km, map, row_mask, flags, tmp);
+  if (st != SC_OK) {
+    free_kmap(h, km);
+    return st;
+  }
+  *out = km;
+  return SC_OK;
+}
+
+sc_status build_down2(Handle* h, const int32_t* coords, int64_t n, uint32_t flags, KMap** out) {
+  KMap* km = nullptr;
+  sc_status st = new_kmap(h, SC_KMAP_DOWN2, 8, n, 0, &km);
+  if (st != SC_OK) return st;
+  Temps tmp(h);
+  if (n == 0) {
+    st = alloc_kmap(h, km);
+    if (st != SC_OK) free_kmap(h, km); else *out = km;
+    return st;
+  }
+  int hmax[4];
+  st = read_maxima(h, coords, n, 1, km->err, tmp, hmax);
+  if (st != SC_OK) {
+    free_kmap(h, km);
+    return st;
+  }
+  Packing pk{bit_width(hmax[1]), bit_width(hmax[2]), bit_width(hmax[3]), hmax[1], hmax[2], hmax[3]};
+  const int bits = std::max(1, bit_width(hmax[0]) + pk.wx + pk.wy + pk.wz);
+  const int passes = (bits + 7) / 8;
+  const size_t tb = radix_sort_temp_bytes(n, 8, passes);
+  unsigned long long *keys, *keys_alt;
+  uint32_t *vals, *vals_alt, *pid, *bsums, *dtotal;
+  void* temp;
+  const int64_t nb = (n + kScanBlock - 1) / kScanBlock;
+  cudaError_t e = tmp.get(&keys, 8 * n);
+  if (e == cudaSuccess) e = tmp.get(&keys_alt, 8 * n);
+  if (e == cudaSuccess) e = tmp.get(&vals, 4 * n);
+  if (e == cudaSuccess) e = tmp.get(&vals_alt, 4 * n);
+  if (e == cudaSuccess) e = tmp.get(&temp, tb);
+  if (e == cudaSuccess) e = tmp.get(&pid, 4 * n);
+  if (e == cudaSuccess) e = tmp.get(&bsums, 4 * nb);
+  if (e == cudaSuccess) e = tmp.get(&dtotal, 16);
+  if (e == cudaSuccess) e = dev_alloc(h, reinterpret_cast<void**>(&km->parent_of), 4 * n);
+  if (e != cudaSuccess) {
+    free_kmap(h, km);
+    return cuda_error(h, e, "alloc down buffers");
+  }
+  const int4* c4 = reinterpret_cast<const int4*>(coords);
+  k_pack_keys<<<blocks_for(n, 256), 256, 0, h->stream>>>(c4, n, 1, pk, keys, vals);
+  bool in_alt = false;
+  st = radix_sort_pairs_u64(h, reinterpret_cast<uint64_t*>(keys), vals, reinterpret_cast<uint64_t*>(keys_alt),
+                            vals_alt, n, 0, bits, temp, tb, km->err, &in_alt);
+  if (st != SC_OK) {
+    free_kmap(h, km);
+    return st;
+  }
+  const unsigned long long* sk = in_alt ? keys_alt : keys;
+  const uint32_t* sv = in_alt ? vals_alt : vals;
+  k_heads_count<<<static_cast<unsigned>(nb), 256, 0, h->stream>>>(sk, n, bsums);
+  k_scan_block_sums<<<1, 1024, 0, h->stream>>>(bsums, nb, dtotal);
+  k_heads_assign<<<static_cast<unsigned>(nb), 1024, 0, h->stream>>>(sk, n, bsums, pid);
+  uint32_t np = 0;
+  e = cudaMemcpyAsync(&np, dtotal, 4, cudaMemcpyDeviceToHost, h->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
+  if (e != cudaSuccess) {
+    free_kmap(h, km);
+    return cuda_error(h, e, "down-sample parent count");
+  }
+  km->n_out = np;
+  st = alloc_kmap(h, km);
+  if (st != SC_OK) {
+    free_kmap(h, km);
+    return st;
+  }
+  int32_t* dmap;
+  uint32_t* row_mask;
+  e = tmp.get(&dmap, sizeof(int32_t) * 8 * np);
+  if (e == cudaSuccess) e = tmp.get(&row_mask, sizeof(uint32_t) * np);
+  if (e == cudaSuccess) e = dev_alloc(h, reinterpret_cast<void**>(&km->out_coords), sizeof(int32_t) * 4 * np);
+  if (e == cudaSuccess) e = cudaMemsetAsync(dmap, 0xFF, sizeof(int32_t) * 8 * np, h->stream);
+  if (e != cudaSuccess) {
+    free_kmap(h, km);
+    return cuda_error(h, e, "alloc down map");
+  }
+  k_down_fill<<<blocks_for(n, 256), 256, 0, h->stream>>>(sk, sv, pid, c4, n, dmap, km->out_coords, km->parent_of,
+                                                          km->err);
+  k_row_masks<<<blocks_for(np, 256), 256, 0, h->stream>>>(dmap, np, 8, row_mask, km->counters);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    free_kmap(h, km);
+    return cuda_error(h, e, "down map launch");
+  }
+  st = finish_tiles(h, km, dmap, row_mask, flags, tmp);
+  if (st != SC_OK) {
+    free_kmap(h, km);
+    return st;
+  }
+  *out = km;
+  return SC_OK;
+}
+
+sc_status build_up2(Handle* h, const KMap* down, uint32_t flags, KMap** out) {
+  if (!down || down->kind != SC_KMAP_DOWN2) return set_error(h, SC_EINVAL, "up2 needs a down2 map");
+  KMap* km = nullptr;
+  sc_status st = new_kmap(h, SC_KMAP_UP2, 8, down->n_out, down->n_in, &km);
+  if (st != SC_OK) return st;
+  Temps tmp(h);
+  st = alloc_kmap(h, km);
+  if (st != SC_OK || km->n_out == 0) {
+    if (st != SC_OK) free_kmap(h, km); else *out = km;
+    return st;
+  }
+  const int64_t n = km->n_out;
+  int32_t* umap;
+  uint32_t* row_mask;
+  cudaError_t e = tmp.get(&umap, sizeof(int32_t) * 8 * n);
+  if (e == cudaSuccess) e = tmp.get(&row_mask, sizeof(uint32_t) * n);
+  if (e == cudaSuccess) e = cudaMemsetAsync(umap, 0xFF, sizeof(int32_t) * 8 * n, h->stream);
+  if (e != cudaSuccess) {
+    free_kmap(h, km);
+    return cuda_error(h, e, "alloc up map");
+  }
+  k_up_fill<<<blocks_for(n, 256), 256, 0, h->stream>>>(down->parent_of, n, umap, row_mask);
+  k_row_masks<<<blocks_for(n, 256), 256, 0, h->stream>>>(umap, n, 8, row_mask, km->counters);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    free_kmap(h, km);
+    return cuda_error(h, e, "up map launch");
+  }
+  st = finish_tiles(h, km, umap, row_mask, flags, tmp);
+  if (st != SC_OK) {
+    free_kmap(h, km);
+    return st;
+  }
+  *out = km;
+  return SC_OK;
+}
+
+sc_status export_map(Handle* h, const KMap* km, int32_t* map_out) {
+  const int64_t n = km->n_out;
+  if (n == 0) return SC_OK;
+  cudaError_t e = cudaMemsetAsync(map_out, 0xFF, sizeof(int32_t) * n * km->K, h->stream);
+  if (e != cudaSuccess) return cuda_error(h, e, "export memset");
+  const int64_t tot = km->num_tiles * km->K * kTileRows;
+  k_export<<<blocks_for(tot, 256), 256, 0, h->stream>>>(km->gidx, km->tile_rows, km->num_tiles, km->K, map_out);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? SC_OK : cuda_error(h, e, "export launch");
+}
+
+void free_kmap(Handle* h, KMap* km) {
+  if (!km) return;
+  dev_free(h, km->gidx);
+  dev_free(h, km->tile_rows);
+  dev_free(h, km->tile_mask);
+  dev_free(h, km->out_coords);
+  dev_free(h, km->parent_of);
+  dev_free(h, km->counters);
+  delete km;
+}
+
+}  // namespace sc

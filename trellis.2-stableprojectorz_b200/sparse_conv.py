@@ -1,0 +1,397 @@
+"""Host-side mirror of the reference sparse-conv operator, backed by the C ABI.
+
+The names follow the reference:
+
+* ``SparseTensor`` -- coords ``(N, 4)`` int32 ``[b, x, y, z]``, feats ``(N, C)``,
+  a scale-keyed spatial cache shared by ``replace()``
+  (``src/sparse/sparse_tensor.ts:18-121``).
+* ``SparseConv3d(weight, bias, kernel_size, dilation).forward(x)`` -- weight in
+  the checkpoint layout ``(Co, Kd, Kh, Kw, Ci)``; the neighbour map is cached in
+  ``x``'s spatial cache under ``conv_neighbors_{Kw}x{Kh}x{Kd}_dil{..}`` exactly
+  like ``src/sparse/ops/conv3d.ts:63-72,144-148``; returns ``x.replace(out)``.
+* ``sparse_conv3d_forward(feats, coords, weight, bias)`` -- the function-level
+  entry a ``SPARSE_CONV_BACKEND`` module exposes (the role of ``conv_none.py``).
+
+Everything runs on the CUDA library; there is no CPU path.  Errors from the
+library surface as ``SparseConvError`` (``DuplicateCoordError`` /
+``CoordRangeError`` for bad coordinates).
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib as L
+from ._lib import SparseConvError, DuplicateCoordError, CoordRangeError  # noqa: F401
+
+__all__ = [
+    "Engine", "get_engine", "KernelMap", "build_kmap", "build_down2", "build_up2", "conv3d",
+    "SparseTensor", "SparseConv3d", "SparseConvDown2", "SparseConvUp2", "sparse_conv3d_forward",
+    "sparse_resblock", "layernorm_silu",
+]
+
+_DTYPES = {torch.float32: L.SC_F32, torch.bfloat16: L.SC_BF16, torch.float16: L.SC_F16}
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(None)
+
+
+class Engine:
+    """One library handle per CUDA device (``sc_create``); binds torch's current stream per call."""
+
+    def __init__(self, device=None, map_mode="hash", debug_bounds=False):
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        if dev.type != "cuda":
+            raise ValueError("the sparse-conv engine runs on CUDA devices only")
+        self.device = torch.device("cuda", dev.index if dev.index is not None else torch.cuda.current_device())
+        self.lib = L.lib()
+        cfg = L.ScConfig()
+        self.lib.sc_config_default(ctypes.byref(cfg))
+        cfg.device = self.device.index
+        cfg.map_mode = {"hash": L.SC_MAP_HASH, "sort": L.SC_MAP_SORT}[map_mode]
+        cfg.debug_bounds = 1 if debug_bounds else 0
+        h = ctypes.c_void_p()
+        st = self.lib.sc_create(ctypes.byref(h), ctypes.byref(cfg))
+        if st != L.SC_OK:
+            raise SparseConvError(st, f"sc_create failed on {self.device}")
+        self.handle = h
+        self.map_mode = map_mode
+
+    def bind_stream(self, stream=None):
+        s = torch.cuda.current_stream(self.device) if stream is None else stream
+        self.lib.sc_set_stream(self.handle, ctypes.c_void_p(s.cuda_stream))
+
+    def check(self, status, what=""):
+        L.check(status, self.handle, what)
+
+    def synchronize(self):
+        self.check(self.lib.sc_synchronize(self.handle), "synchronize")
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.sc_destroy(self.handle)
+            self.handle = None
+
+
+_engines = {}
+_engines_lock = threading.Lock()
+
+
+def get_engine(device=None, map_mode="hash"):
+    """Cached Engine for ``(device, map_mode)``."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    key = (idx, map_mode)
+    with _engines_lock:
+        if key not in _engines:
+            _engines[key] = Engine(torch.device("cuda", idx), map_mode)
+        return _engines[key]
+
+
+class KernelMap:
+    """A built neighbour / gather map (``sc_kmap*``), freed with the object."""
+
+    def __init__(self, engine, ptr, kind, keepalive=None):
+        self.engine = engine
+        self.ptr = ptr
+        self.kind = kind
+        self._keepalive = keepalive
+        info = self.info()
+        self.n_in = info["n_in"]
+        self.n_out = info["n_out"]
+        self.kernel_volume = info["kernel_volume"]
+
+    def info(self):
+        inf = L.ScKmapInfo()
+        self.engine.check(self.engine.lib.sc_kmap_get_info(self.engine.handle, self.ptr, ctypes.byref(inf)),
+                          "sc_kmap_get_info")
+        return {k: getattr(inf, k) for k, _ in L.ScKmapInfo._fields_}
+
+    def check(self):
+        self.engine.check(self.engine.lib.sc_kmap_check(self.engine.handle, self.ptr), "sc_kmap_check")
+
+    def export(self):
+        """Canonical ``[n_out, K]`` int32 map on the device."""
+        out = torch.empty((self.n_out, self.kernel_volume), dtype=torch.int32, device=self.engine.device)
+        self.engine.bind_stream()
+        self.engine.check(self.engine.lib.sc_kmap_export(self.engine.handle, self.ptr, _ptr(out)), "sc_kmap_export")
+        return out
+
+    def out_coords(self):
+        """Parent coords of a down-sample map, ``[n_out, 4]`` int32."""
+        out = torch.empty((self.n_out, 4), dtype=torch.int32, device=self.engine.device)
+        self.engine.bind_stream()
+        self.engine.check(self.engine.lib.sc_kmap_out_coords(self.engine.handle, self.ptr, _ptr(out)),
+                          "sc_kmap_out_coords")
+        return out
+
+    def free(self):
+        if self.ptr is not None and self.engine.handle:
+            self.engine.bind_stream()
+            self.engine.lib.sc_kmap_free(self.engine.handle, self.ptr)
+        self.ptr = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def _coords_arg(coords):
+    if coords.dtype != torch.int32 or coords.dim() != 2 or coords.shape[1] != 4:
+        raise ValueError("coords must be an (N, 4) int32 tensor [b, x, y, z]")
+    if not coords.is_cuda:
+        raise ValueError("coords must be on a CUDA device")
+    return coords.contiguous()
+
+
+def _flags(tile_sort, check):
+    f = 0 if tile_sort else L.SC_BUILD_NO_TILE_SORT
+    return f if check else f | L.SC_BUILD_DEFER_CHECK
+
+
+def build_kmap(coords, dilation=1, engine=None, tile_sort=True, check=True):
+    """Submanifold 3x3x3 neighbour map (``sc_kmap_build``)."""
+    coords = _coords_arg(coords)
+    eng = engine or get_engine(coords.device)
+    eng.bind_stream()
+    p = ctypes.c_void_p()
+    eng.check(eng.lib.sc_kmap_build(eng.handle, _ptr(coords), coords.shape[0], 3, int(dilation),
+                                    _flags(tile_sort, check), ctypes.byref(p)), "sc_kmap_build")
+    return KernelMap(eng, p, L.SC_KMAP_SUBM)
+
+
+def build_down2(coords, engine=None, tile_sort=True):
+    """Stride-2 2x2x2 down-sample map (``sc_kmap_build_down2``)."""
+    coords = _coords_arg(coords)
+    eng = engine or get_engine(coords.device)
+    eng.bind_stream()
+    p = ctypes.c_void_p()
+    eng.check(eng.lib.sc_kmap_build_down2(eng.handle, _ptr(coords), coords.shape[0], _flags(tile_sort, True),
+                                          ctypes.byref(p)), "sc_kmap_build_down2")
+    return KernelMap(eng, p, L.SC_KMAP_DOWN2)
+
+
+def build_up2(down, tile_sort=True):
+    """Transposed map of a down-sample map (``sc_kmap_build_up2``)."""
+    eng = down.engine
+    eng.bind_stream()
+    p = ctypes.c_void_p()
+    eng.check(eng.lib.sc_kmap_build_up2(eng.handle, down.ptr, _flags(tile_sort, True), ctypes.byref(p)),
+              "sc_kmap_build_up2")
+    return KernelMap(eng, p, L.SC_KMAP_UP2, keepalive=down)
+
+
+def conv3d(kmap, feats, weight, bias=None, residual=None, silu=False, layernorm=False, eps=1e-6, out=None):
+    """``out = epilogue(bias + sum_v W[:, v] . feats[map[:, v]])`` through ``sc_conv3d``."""
+    dt = _DTYPES.get(feats.dtype)
+    if dt is None:
+        raise TypeError(f"unsupported feature dtype {feats.dtype}")
+    co, ci = int(weight.shape[0]), int(weight.shape[-1])
+    if weight.numel() != co * ci * kmap.kernel_volume:
+        raise ValueError(f"weight {tuple(weight.shape)} does not match a {kmap.kernel_volume}-offset kernel")
+    if feats.shape != (kmap.n_in, ci):
+        raise ValueError(f"feats {tuple(feats.shape)} != ({kmap.n_in}, {ci})")
+    feats = feats.contiguous()
+    weight = weight.to(feats.dtype).contiguous()
+    if bias is not None:
+        bias = bias.to(feats.dtype).contiguous()
+    if residual is not None:
+        residual = residual.to(feats.dtype).contiguous()
+        if residual.shape != (kmap.n_out, co):
+            raise ValueError("residual must be (n_out, Co)")
+    if out is None:
+        out = torch.empty((kmap.n_out, co), dtype=feats.dtype, device=feats.device)
+    epi = (L.SC_EPI_SILU if silu else 0) | (L.SC_EPI_RESIDUAL if residual is not None else 0) | \
+          (L.SC_EPI_LAYERNORM if layernorm else 0)
+    eng = kmap.engine
+    eng.bind_stream()
+    eng.check(eng.lib.sc_conv3d(eng.handle, kmap.ptr, _ptr(feats), _ptr(weight), _ptr(bias), _ptr(residual),
+                                _ptr(out), ci, co, dt, epi, float(eps)), "sc_conv3d")
+    return out
+
+
+def layernorm_silu(x, silu=True, eps=1e-6, engine=None):
+    """In-place row LayerNorm (no affine) + optional SiLU."""
+    eng = engine or get_engine(x.device)
+    eng.bind_stream()
+    eng.check(eng.lib.sc_layernorm_silu(eng.handle, _ptr(x), x.shape[0], x.shape[1], _DTYPES[x.dtype],
+                                        1 if silu else 0, float(eps)), "sc_layernorm_silu")
+    return x
+
+
+class SparseTensor:
+    """Sparse voxels: coords ``(N, 4)`` int32 ``[b, x, y, z]`` + feats ``(N, C)``.
+
+    Mirrors ``src/sparse/sparse_tensor.ts:18-121``: the spatial cache is a dict
+    keyed by scale and shared by ``replace()``, so every conv on the same
+    coords reuses one neighbour map.
+    """
+
+    def __init__(self, feats, coords, shape=None, scale=(1, 1, 1), cache=None):
+        self.feats = feats
+        self.coords = coords
+        self._shape = shape
+        self._scale = tuple(scale)
+        self._spatial_cache = {} if cache is None else cache
+
+    @property
+    def scale(self):
+        return self._scale
+
+    @property
+    def device(self):
+        return self.feats.device
+
+    @property
+    def dtype(self):
+        return self.feats.dtype
+
+    def get_spatial_cache(self, key):
+        return self._spatial_cache.get(self._scale, {}).get(key)
+
+    def register_spatial_cache(self, key, value):
+        self._spatial_cache.setdefault(self._scale, {})[key] = value
+
+    def clear_spatial_cache(self):
+        self._spatial_cache.clear()
+
+    def replace(self, feats, coords=None):
+        if coords is None:
+            return SparseTensor(feats, self.coords, self._shape, self._scale, self._spatial_cache)
+        return SparseTensor(feats, coords, None, self._scale, None)
+
+    @property
+    def spatial_shape(self):
+        s = self.get_spatial_cache("shape")
+        if s is None:
+            s = tuple(int(v) + 1 for v in self.coords[:, 1:].amax(0).tolist()) if self.coords.shape[0] else (0, 0, 0)
+            self.register_spatial_cache("shape", s)
+        return s
+
+    def __repr__(self):
+        return f"SparseTensor(voxels={self.feats.shape[0]}, channels={self.feats.shape[1]}, dtype={self.dtype})"
+
+
+class SparseConv3d:
+    """Submanifold sparse conv (3x3x3), the drop-in for ``SparseConv3d`` of
+    ``src/sparse/ops/conv3d.ts:18-222``.
+
+    ``weight``: ``(Co, 3, 3, 3, Ci)``; ``bias``: ``(Co,)`` or None.
+    """
+
+    def __init__(self, weight, bias=None, kernel_size=(3, 3, 3), dilation=(1, 1, 1)):
+        ks = tuple(kernel_size) if not isinstance(kernel_size, int) else (kernel_size,) * 3
+        dl = tuple(dilation) if not isinstance(dilation, int) else (dilation,) * 3
+        if ks != (3, 3, 3):
+            raise NotImplementedError("only 3x3x3 submanifold kernels are implemented")
+        if len(set(dl)) != 1:
+            raise NotImplementedError("anisotropic dilation is not implemented")
+        if weight.dim() != 5 or tuple(weight.shape[1:4]) != ks:
+            raise ValueError("weight must be (Co, Kd, Kh, Kw, Ci)")
+        self.weight = weight
+        self.bias = bias
+        self.kernel_size = ks
+        self.dilation = dl
+
+    @property
+    def V(self):
+        return self.kernel_size[0] * self.kernel_size[1] * self.kernel_size[2]
+
+    def cache_key(self):
+        kd, kh, kw = self.kernel_size
+        dd, dh, dw = self.dilation
+        return f"conv_neighbors_{kw}x{kh}x{kd}_dil{dw}x{dh}x{dd}"
+
+    def neighbour_map(self, x):
+        km = x.get_spatial_cache(self.cache_key())
+        if km is None:
+            km = build_kmap(x.coords, self.dilation[0])
+            x.register_spatial_cache(self.cache_key(), km)
+        return km
+
+    def forward(self, x, silu=False, residual=None):
+        if not x.feats.is_cuda:
+            raise ValueError("SparseConv3d requires GPU input")
+        km = self.neighbour_map(x)
+        out = conv3d(km, x.feats, self.weight, self.bias, residual=residual, silu=silu)
+        return x.replace(out)
+
+    __call__ = forward
+
+
+class SparseConvDown2:
+    """Stride-2 2x2x2 sparse conv: ``weight (Co, 2, 2, 2, Ci)``.
+
+    Output coords are the unique ``(b, x>>1, y>>1, z>>1)`` in ascending
+    lexicographic order.  The down map is cached on the input's spatial cache
+    and handed to the output so that ``SparseConvUp2`` can return to the fine
+    coords.
+    """
+
+    def __init__(self, weight, bias=None):
+        if weight.dim() != 5 or tuple(weight.shape[1:4]) != (2, 2, 2):
+            raise ValueError("weight must be (Co, 2, 2, 2, Ci)")
+        self.weight = weight
+        self.bias = bias
+
+    def forward(self, x, silu=False):
+        km = x.get_spatial_cache("down2_map")
+        if km is None:
+            km = build_down2(x.coords)
+            x.register_spatial_cache("down2_map", km)
+        out = conv3d(km, x.feats, self.weight, self.bias, silu=silu)
+        coarse = SparseTensor(out, km.out_coords(), None, tuple(2 * s for s in x.scale))
+        coarse.register_spatial_cache("up2_source", (km, x))
+        return coarse
+
+    __call__ = forward
+
+
+class SparseConvUp2:
+    """Transposed 2x2x2 sparse conv back onto the fine coords of the matching
+    ``SparseConvDown2`` input: ``out[c] = bias + W[:, slot(c), :] . g[parent(c)]``."""
+
+    def __init__(self, weight, bias=None):
+        if weight.dim() != 5 or tuple(weight.shape[1:4]) != (2, 2, 2):
+            raise ValueError("weight must be (Co, 2, 2, 2, Ci)")
+        self.weight = weight
+        self.bias = bias
+
+    def forward(self, x, silu=False):
+        src = x.get_spatial_cache("up2_source")
+        if src is None:
+            raise ValueError("SparseConvUp2 needs a tensor produced by SparseConvDown2")
+        down, fine = src
+        km = fine.get_spatial_cache("up2_map")
+        if km is None:
+            km = build_up2(down)
+            fine.register_spatial_cache("up2_map", km)
+        out = conv3d(km, x.feats, self.weight, self.bias, silu=silu)
+        return fine.replace(out)
+
+    __call__ = forward
+
+
+def sparse_conv3d_forward(feats, coords, weight, bias=None, dilation=1, kmap=None):
+    """Function-level submanifold conv for a ``SPARSE_CONV_BACKEND`` module.
+
+    Returns ``(out, kmap)``; pass ``kmap`` back in to reuse the neighbour map
+    for later layers on the same coords.
+    """
+    if kmap is None:
+        kmap = build_kmap(coords, dilation)
+    return conv3d(kmap, feats, weight, bias), kmap
+
+
+def sparse_resblock(x, w1, b1, w2, b2, eps=1e-6):
+    """conv -> LayerNorm -> SiLU -> conv + identity skip; both convs share one map
+    and the LN/SiLU and the skip add are fused into the conv epilogues."""
+    km = SparseConv3d(w1).neighbour_map(x)
+    h = conv3d(km, x.feats, w1, b1, silu=True, layernorm=True, eps=eps)
+    out = conv3d(km, h, w2, b2, residual=x.feats)
+    return x.replace(out)
