@@ -107,6 +107,9 @@ SC_API sc_status sc_set_stream(sc_handle* h, void* stream);
 SC_API sc_status sc_synchronize(sc_handle* h);
 /* Human-readable description of the last error on this handle. */
 SC_API const char* sc_last_error(const sc_handle* h);
+/* Number of CUDA kernels this handle has launched so far (instrumentation;
+ * no counterpart in the reference). */
+SC_API uint64_t sc_launch_count(const sc_handle* h);
 
 /* Submanifold neighbour map for a 3x3x3 kernel with dilation `dilation`.
  * Replaces passes 0+1 (src/sparse/ops/conv3d.ts:73-151,

@@ -1,0 +1,148 @@
+"""CPU checks of the oracle restatement (no GPU).
+
+The reference documents two invariants for its sparse-conv path
+(README.md:80-81): the neighbour lookup equals brute force, and the sparse
+conv equals dense F.conv3d to 1e-5.  These tests establish both for the
+oracle, then pin it to the committed golden fixtures.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm(np.asarray(a, np.float64) - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.mark.parametrize("cfg,scale", [(1, 1.0), (1, 0.5), (3, 0.3)])
+def test_sorted_map_equals_bruteforce(pkg, oracle, cfg, scale):
+    w = pkg.workloads.make_workload(cfg, scale=scale)
+    perm = pkg.workloads.shuffle_rows(w.n, cfg)
+    c = w.coords[perm]
+    a = oracle.kmap_bruteforce(c, w.spatial_shape, w.batch_size)
+    b = oracle.kmap_sorted(c, w.spatial_shape)
+    assert np.array_equal(a, b)
+    # centre column is the row itself; symmetric offsets are inverse maps
+    assert np.array_equal(a[:, 13], np.arange(len(c)))
+    for v in range(27):
+        rows = np.where(a[:, v] >= 0)[0]
+        assert np.array_equal(a[a[rows, v], 26 - v], rows)
+
+
+def test_torch_cpu_map_equals_numpy(pkg, oracle):
+    w = pkg.workloads.make_workload(1)
+    a = oracle.kmap_sorted(w.coords, w.spatial_shape)
+    b = oracle.torch_cpu_kmap(torch.from_numpy(w.coords), w.spatial_shape).numpy()
+    assert np.array_equal(a, b)
+
+
+def test_dilated_map(pkg, oracle):
+    w = pkg.workloads.make_workload(1, scale=0.6)
+    for d in (2, 3):
+        assert np.array_equal(oracle.kmap_bruteforce(w.coords, w.spatial_shape, 1, d),
+                              oracle.kmap_sorted(w.coords, w.spatial_shape, d))
+
+
+def test_duplicates_rejected(pkg, oracle):
+    w = pkg.workloads.make_workload(1, scale=0.5)
+    c = np.concatenate([w.coords, w.coords[:1]], 0)
+    with pytest.raises(ValueError):
+        oracle.kmap_sorted(c, w.spatial_shape)
+    with pytest.raises(ValueError):
+        oracle.kmap_bruteforce(c, w.spatial_shape, 1)
+
+
+def test_conv_matches_dense_conv3d(pkg, oracle):
+    w = pkg.workloads.make_workload(1)
+    rng = np.random.default_rng(3)
+    f = rng.standard_normal((w.n, 8)).astype(np.float32)
+    W = (rng.standard_normal((8, 3, 3, 3, 8)) / 14).astype(np.float32)
+    b = (0.1 * rng.standard_normal(8)).astype(np.float32)
+    km = oracle.kmap_sorted(w.coords, w.spatial_shape)
+    sparse = oracle.conv_gather(f, km, W, b)
+    dense = oracle.dense_conv3d_check(w.coords, f, W, b, w.spatial_shape, 1)
+    assert rel_l2(sparse, dense) < 1e-12  # both float64
+    # torch-CPU f32 version used for the CPU baseline
+    t = oracle.torch_cpu_conv(torch.from_numpy(f), torch.from_numpy(km), torch.from_numpy(W), torch.from_numpy(b))
+    assert rel_l2(t.numpy(), dense) < 1e-5
+
+
+def test_down_conv_matches_strided_dense(pkg, oracle):
+    w = pkg.workloads.make_workload(4, scale=0.04)
+    rng = np.random.default_rng(5)
+    f = rng.standard_normal((w.n, 4)).astype(np.float64)
+    W = rng.standard_normal((6, 2, 2, 2, 4))
+    pc, dmap = oracle.down2_map(w.coords)
+    sparse = oracle.conv_gather(f, dmap, W)
+    c = torch.as_tensor(w.coords.astype(np.int64))
+    X = int(c[:, 1:].max()) + 2
+    X += X % 2
+    dense = torch.zeros((1, 4, X, X, X), dtype=torch.float64)
+    dense[c[:, 0], :, c[:, 1], c[:, 2], c[:, 3]] = torch.as_tensor(f)
+    y = F.conv3d(dense, torch.as_tensor(W).permute(0, 4, 1, 2, 3), stride=2)
+    p = torch.as_tensor(pc.astype(np.int64))
+    ref = y[p[:, 0], :, p[:, 1], p[:, 2], p[:, 3]].numpy()
+    assert rel_l2(sparse, ref) < 1e-12
+    # parents are unique and in ascending lexicographic order
+    keys = ((pc[:, 0].astype(np.int64) * 65536 + pc[:, 1]) * 65536 + pc[:, 2]) * 65536 + pc[:, 3]
+    assert np.all(np.diff(keys) > 0)
+
+
+def test_up_conv_matches_transposed_dense(pkg, oracle):
+    w = pkg.workloads.make_workload(4, scale=0.04)
+    rng = np.random.default_rng(6)
+    pc, _ = oracle.down2_map(w.coords)
+    g = rng.standard_normal((len(pc), 5))
+    W = rng.standard_normal((3, 2, 2, 2, 5))
+    umap = oracle.up2_map(w.coords, pc)
+    sparse = oracle.conv_gather(g, umap, W)
+    p = torch.as_tensor(pc.astype(np.int64))
+    Xc = int(p[:, 1:].max()) + 1
+    dense = torch.zeros((1, 5, Xc, Xc, Xc), dtype=torch.float64)
+    dense[p[:, 0], :, p[:, 1], p[:, 2], p[:, 3]] = torch.as_tensor(g)
+    y = F.conv_transpose3d(dense, torch.as_tensor(W).permute(4, 0, 1, 2, 3), stride=2)
+    c = torch.as_tensor(w.coords.astype(np.int64))
+    ref = y[c[:, 0], :, c[:, 1], c[:, 2], c[:, 3]].numpy()
+    assert rel_l2(sparse, ref) < 1e-12
+    assert np.all((umap >= 0).sum(1) == 1)
+
+
+def test_layernorm_silu_match_torch(oracle):
+    x = np.random.default_rng(1).standard_normal((50, 32))
+    ln = torch.nn.functional.layer_norm(torch.as_tensor(x), (32,), eps=1e-6).numpy()
+    assert rel_l2(oracle.layer_norm(x, 1e-6), ln) < 1e-12
+    assert rel_l2(oracle.silu(x), torch.nn.functional.silu(torch.as_tensor(x)).numpy()) < 1e-12
+
+
+def test_golden_fixtures_pin_the_oracle(oracle):
+    d = np.load(os.path.join(GOLDEN, "subm_c1_small.npz"))
+    shape = tuple(d["spatial_shape"])
+    km = oracle.kmap_sorted(d["coords"], shape)
+    assert np.array_equal(km, d["kmap"])
+    assert np.array_equal(km, oracle.kmap_bruteforce(d["coords"], shape, 1))
+    assert np.array_equal(oracle.kmap_sorted(d["coords"], shape, 2), d["kmap_dil2"])
+    assert rel_l2(oracle.conv_gather(d["feats"], km, d["weight"], d["bias"]), d["out"]) < 1e-6
+    d2 = np.load(os.path.join(GOLDEN, "subm_batch2.npz"))
+    assert np.array_equal(oracle.kmap_bruteforce(d2["coords"], (64, 64, 64), 2), d2["kmap"])
+    d3 = np.load(os.path.join(GOLDEN, "downup_c4_small.npz"))
+    pc, dmap = oracle.down2_map(d3["coords"])
+    assert np.array_equal(pc, d3["parent_coords"]) and np.array_equal(dmap, d3["dmap"])
+    assert np.array_equal(oracle.up2_map(d3["coords"], pc), d3["umap"])
+    assert rel_l2(oracle.conv_gather(d3["feats"], dmap, d3["w_down"]), d3["out_down"]) < 1e-6
+
+
+def test_workloads_are_deterministic_and_valid(pkg):
+    for cfg, scale in [(1, 1.0), (2, 0.2), (3, 0.2), (4, 0.05)]:
+        a = pkg.workloads.make_workload(cfg, scale=scale)
+        b = pkg.workloads.make_workload(cfg, scale=scale)
+        assert np.array_equal(a.coords, b.coords) and np.array_equal(a.feats, b.feats)
+        c = a.coords.astype(np.int64)
+        key = ((c[:, 0] * 65536 + c[:, 1]) * 65536 + c[:, 2]) * 65536 + c[:, 3]
+        assert len(np.unique(key)) == len(c)
+        assert c.min() >= 0 and c[:, 1:].max() < a.spatial_shape[0]
+        assert np.all(np.diff(c[:, 0]) >= 0)  # batch-sorted

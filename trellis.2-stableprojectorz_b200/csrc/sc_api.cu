@@ -180,6 +180,8 @@ const char* sc_last_error(const sc_handle* h) {
   return h->impl.last_error.c_str();
 }
 
+uint64_t sc_launch_count(const sc_handle* h) { return h ? h->impl.launches : 0; }
+
 sc_status sc_kmap_build(sc_handle* h, const int32_t* coords, int64_t n, int32_t kernel_size, int32_t dilation,
                         uint32_t flags, sc_kmap** out) {
   if (!h || !out) return SC_EINVAL;

@@ -132,6 +132,7 @@ template <typename T>
 sc_status launch_rownorm(Handle* h, void* x, int64_t n, int c, float eps, int ln, int silu, const void* res) {
   const int rows_per_block = 8;
   const unsigned grid = static_cast<unsigned>((n + rows_per_block - 1) / rows_per_block);
+  ++h->launches;
   k_rownorm<T><<<grid, rows_per_block * 32, 0, h->stream>>>(static_cast<T*>(x), n, c, eps, ln, silu,
                                                             static_cast<const T*>(res));
   const cudaError_t e = cudaGetLastError();
@@ -163,6 +164,7 @@ sc_status conv_simt_f32(Handle* h, const KMap* km, const float* feats, const flo
   // With LayerNorm the conv writes bias-added rows and the row kernel applies
   // LN -> SiLU -> residual; otherwise the epilogue is fused.
   const bool ln = (epi & SC_EPI_LAYERNORM) != 0;
+  ++h->launches;
   k_conv_simt_f32<<<static_cast<unsigned>(blocks), 256, 0, h->stream>>>(
       km->gidx, km->tile_rows, km->tile_mask, km->K, co_blocks, feats, weight, bias, residual, out, ci, co,
       ln ? 0u : epi);

@@ -3,17 +3,20 @@
 // Implicit GEMM over the kernel map: for each 128-row output tile and each
 // neighbour offset v present in the tile,
 //     D[128, bn] += gather(feats, gidx[t][v])[128, Ci] . W[:, v, :]^T
-// with the gather done by TMA tile::gather4 (four rows per instruction, rows
-// of -1 are zero-filled by the TMA unit) and W[:, v, kc] by a tiled TMA load,
-// both into 128B/64B/32B-swizzled shared memory that tcgen05.mma reads
-// directly.  The accumulator lives in TMEM (two buffers, so the epilogue of
-// one tile overlaps the main loop of the next).  The epilogue adds bias and
-// optionally LayerNorm / SiLU / residual and stores bf16/f16 rows.
+// The gathered rows are copied with 16-byte cp.async by four producer warps
+// straight into the 128B/64B/32B-swizzled K-major layout (rows of -1 are
+// zero-filled); W[:, v, kc] arrives by a tiled TMA load.  tcgen05.mma reads
+// both from shared memory and accumulates in TMEM (two buffers, so the
+// epilogue of one tile overlaps the main loop of the next).  The epilogue adds
+// bias and optionally LayerNorm / SiLU / residual and stores bf16/f16 rows.
 //
-// Warp roles (192 threads, one persistent CTA per SM):
-//   warp 0     TMA producer (all 32 lanes issue one gather4 each per stage)
-//   warp 1     TMEM allocator + single-thread MMA issuer
-//   warps 2-5  epilogue (warp w reads TMEM lanes 32*(w%4) .. +31)
+// Warp roles (288 threads, one persistent CTA per SM):
+//   warps 0-3  producers: per tile, stage the tile's gather indices in shared
+//              memory (double-buffered, prefetched one tile ahead), then per
+//              (offset, K-chunk) stage issue the row copies; thread 0 also
+//              issues the weight TMA
+//   warp 4     TMEM allocator + single-thread MMA issuer
+//   warps 5-8  epilogue (warp w reads TMEM lanes 32*(w%4) .. +31)
 //
 // Reference math: src/sparse/ops/conv3d_wgsl.ts:177-222 (pass 2), weight
 // layout (Co,Kd,Kh,Kw,Ci) from src/sparse/ops/conv3d.ts:5,48-49.  No TMA
@@ -46,10 +49,12 @@ struct TcParams {
   const int32_t* gidx;
   const int32_t* tile_rows;
   const uint32_t* tile_mask;
+  const void* feats;
   const void* bias;
   const void* residual;
   void* out;
-  int64_t num_items;  // tiles * co_blocks
+  int64_t num_items;  // tile groups * co_blocks
+  int64_t num_tiles;
   int co_blocks;
   int K;
   int ci;
@@ -61,19 +66,31 @@ struct TcParams {
   int* err;
 };
 
-constexpr int kTcThreads = 192;
+constexpr int kProducers = 128;  // warps 0-3
+constexpr int kMmaWarp = 4;
+constexpr int kTcThreads = 288;
 
-template <int KC, int BNMAX>
+// Shared-memory plan for one CTA.  A stage holds TPI gathered A tiles
+// (128 rows x KC each) and one weight tile (BNMAX rows x KC) that all TPI
+// tiles multiply, so weight traffic per output row drops by TPI.
+template <int KC, int BNMAX, int TPI>
 struct TcShape {
-  static constexpr int kABytes = 128 * KC * 2;
+  static constexpr int kABytes = 128 * KC * 2;  // one tile's A operand
   static constexpr int kBBytes = BNMAX * KC * 2;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStagesFit = (192 * 1024) / kStageBytes;
+  static constexpr int kStageBytes = TPI * kABytes + kBBytes;
+  static constexpr int kOutBytes = 4 * 32 * 32 * 2;  // epilogue staging: per warp 32 rows x 32 columns
+  static constexpr int kIdxBytes = 27 * 128 * TPI * 4;  // gather indices of the tile group being produced
+  static constexpr int kStageBudget = 224 * 1024 - kIdxBytes - kOutBytes - 2048;
+  static constexpr int kStagesFit = kStageBudget / kStageBytes;
   static constexpr int kStages = kStagesFit > 12 ? 12 : kStagesFit;
+  static_assert(kStages >= 2, "not enough shared memory for two stages");
+  static constexpr int kAccCols = TPI * BNMAX;  // TMEM columns of one accumulator buffer
   static constexpr uint32_t kTmemCols =
-      (2 * BNMAX <= 32) ? 32 : (2 * BNMAX <= 64) ? 64 : (2 * BNMAX <= 128) ? 128 : (2 * BNMAX <= 256) ? 256 : 512;
+      (2 * kAccCols <= 32) ? 32 : (2 * kAccCols <= 64) ? 64 : (2 * kAccCols <= 128) ? 128 : (2 * kAccCols <= 256) ? 256 : 512;
+  static_assert(2 * kAccCols <= 512, "two accumulator buffers must fit in TMEM");
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kIdxBytes + kOutBytes + kBarBytes + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory plan too large");
   static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment");
   static_assert(2 * kStages + 5 <= 30, "barrier area too small");
 };
@@ -135,10 +152,15 @@ __device__ __forceinline__ float chunk_sum(uint32_t tb, int c0, bool live, const
   return s;
 }
 
-// Epilogue of W columns of one output row: +bias, LayerNorm, SiLU, +residual, store.
+// Epilogue of W columns (32 or 16) of the warp's 32 output rows: +bias,
+// LayerNorm, SiLU, +residual, bf16/f16 pack.  Each lane stages its row
+// segment in the warp's shared-memory buffer (16-byte chunks XOR-swizzled by
+// row pair, conflict-free), then the warp writes the segments back with each store instruction
+// covering whole row segments of several rows, not 16 bytes of 32 rows.
 template <typename T, int W>
 __device__ __forceinline__ void epi_chunk(uint32_t tb, int c0, bool live, const T* bias, const T* res, T* out,
-                                          int r, int co, int col0, float mean, float rstd, uint32_t epi) {
+                                          int r, int co, int col0, float mean, float rstd, uint32_t epi,
+                                          uint8_t* wbuf, int lane) {
   float v[W];
   tmem_ld<W>(tb + c0, v);
 #pragma unroll
@@ -148,28 +170,52 @@ __device__ __forceinline__ void epi_chunk(uint32_t tb, int c0, bool live, const 
     if (epi & SC_EPI_SILU) x = silu_f(x);
     v[j] = x;
   }
-  if (r >= 0) {
-    const int64_t off = static_cast<int64_t>(r) * co + col0 + c0;
-    if (epi & SC_EPI_RESIDUAL) {
-      float rr[W];
-      load_row<T, W>(res + off, rr);
+  if ((epi & SC_EPI_RESIDUAL) && r >= 0) {
+    float rr[W];
+    load_row<T, W>(res + static_cast<int64_t>(r) * co + col0 + c0, rr);
 #pragma unroll
-      for (int j = 0; j < W; ++j) v[j] += rr[j];
-    }
-    store_row<T, W>(out + off, v);
+    for (int j = 0; j < W; ++j) v[j] += rr[j];
   }
+  constexpr int CH = W / 8;  // 16-byte chunks per row segment (4 or 2)
+#pragma unroll
+  for (int q = 0; q < CH; ++q) {
+    uint32_t w4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+        const __nv_bfloat162 b = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
+        w4[j] = *reinterpret_cast<const uint32_t*>(&b);
+      } else {
+        const __half2 b = __floats2half2_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
+        w4[j] = *reinterpret_cast<const uint32_t*>(&b);
+      }
+    }
+    *reinterpret_cast<uint4*>(wbuf + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+  }
+  __syncwarp();
+  constexpr int RPI = 32 / CH;  // rows per store instruction
+#pragma unroll
+  for (int i = 0; i < 32 / RPI; ++i) {
+    const int lr = i * RPI + lane / CH;  // row within the warp
+    const int ch = lane % CH;
+    const int orow = __shfl_sync(0xffffffffu, r, lr);
+    const uint4 val = *reinterpret_cast<const uint4*>(wbuf + lr * 64 + ((ch ^ ((lr >> 1) & 3)) * 16));
+    if (orow >= 0) *reinterpret_cast<uint4*>(out + static_cast<int64_t>(orow) * co + col0 + c0 + ch * 8) = val;
+  }
+  __syncwarp();
 }
 
-template <int KC, int BNMAX, bool BF16>
+template <int KC, int BNMAX, int TPI, bool BF16>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const TcParams p) {
-  using S = TcShape<KC, BNMAX>;
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmB, const TcParams p) {
+  using S = TcShape<KC, BNMAX, TPI>;
   using Z = SwizzleCfg<KC>;
   using T = std::conditional_t<BF16, __nv_bfloat16, __half>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes);
+  int32_t* idx_s = reinterpret_cast<int32_t*>(smem + S::kStages * S::kStageBytes);  // [27][TPI*128]
+  uint8_t* out_s = smem + S::kStages * S::kStageBytes + S::kIdxBytes;  // [4 warps][32 rows][32 cols]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(out_s + S::kOutBytes);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 30);
   const uint32_t smem_base = smem_u32(smem);
   const uint32_t bar_base = smem_u32(bars);
@@ -182,7 +228,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::kStages; ++s) {
-      mbar_init(full0 + 8u * s, 1);
+      mbar_init(full0 + 8u * s, kProducers + 1);  // one cp.async arrival per producer + the weight TMA
       mbar_init(empty0 + 8u * s, 1);
     }
     mbar_init(tfull0, 1);
@@ -190,11 +236,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_init(tempty0, 128);
     mbar_init(tempty0 + 8u, 128);
     mbar_init(done_bar, 1);
+    s_tmem[1] = 0;  // producer abort flag
     fence_mbar_init();
-    prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(s_tmem), S::kTmemCols);
     tmem_relinquish();
   }
@@ -203,52 +249,131 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
   const int bn = p.bn;
+  // An item is a group of TPI consecutive tiles times one block of bn output
+  // channels; the group runs the union of its tiles' offsets.
+  auto group_mask = [&](int64_t g) {
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < TPI; ++i)
+      if (g * TPI + i < p.num_tiles) m |= __ldg(p.tile_mask + g * TPI + i);
+    return m;
+  };
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    const uint32_t stage_tx = static_cast<uint32_t>(S::kABytes + bn * KC * 2);
+  if (warp < kProducers / 32) {
+    // ------------------------------------------------------------ producers
+    constexpr int CPR = KC / 8;             // 16-byte chunks per gathered row
+    constexpr int RSTEP = 128 / CPR;        // rows between one thread's copies
+    constexpr int ROWB = KC * 2;            // bytes per row in a stage
+    const int pt = threadIdx.x;             // 0..127
+    const int chunk = pt % CPR;
+    const int row0 = pt / CPR;
+    const T* feats = static_cast<const T*>(p.feats);
+    const uint32_t b_tx = static_cast<uint32_t>(bn * KC * 2);
     int stage = 0;
     uint32_t phase = 0;
-    uint32_t used = 0, used_par = 0;  // stages ever filled and the parity of their last fill
-    bool ok = true;
-    for (int64_t item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
-      const int64_t t = item / p.co_blocks;
-      const int cb = static_cast<int>(item - t * p.co_blocks);
-      uint32_t mask = __ldg(p.tile_mask + t);
-      while (ok && mask) {
+    uint32_t used = 0, used_par = 0;  // stages whose weight TMA was issued, parity of the last issue
+    // A timed-out wait sets `abort`; producers then keep walking the same
+    // item sequence without waiting or copying, so the named barrier below is
+    // reached the same number of times by all four warps.
+    bool abort = false;
+    // gather-index prefetch: warp w loads active offsets j = w, w+4, ... (<= 7 each)
+    int4 pre[7][TPI];
+    auto load_idx = [&](int64_t item) {
+      const int64_t g = item / p.co_blocks;
+      const uint32_t m = group_mask(g);
+      const int nact = __popc(m);
+#pragma unroll
+      for (int k = 0; k < 7; ++k) {
+        const int j = warp + 4 * k;
+        if (j < nact) {
+          const int v = __fns(m, 0, j + 1);
+#pragma unroll
+          for (int i = 0; i < TPI; ++i) {
+            const int64_t t = g * TPI + i;
+            pre[k][i] = t < p.num_tiles ? __ldg(reinterpret_cast<const int4*>(p.gidx + (t * p.K + v) * 128) + lane)
+                                        : make_int4(-1, -1, -1, -1);
+          }
+        }
+      }
+      return nact;
+    };
+    auto store_idx = [&](int nact) {
+      int4* dst = reinterpret_cast<int4*>(idx_s);
+#pragma unroll
+      for (int k = 0; k < 7; ++k) {
+        const int j = warp + 4 * k;
+        if (j < nact) {
+#pragma unroll
+          for (int i = 0; i < TPI; ++i) dst[(j * TPI + i) * 32 + lane] = pre[k][i];
+        }
+      }
+    };
+    int64_t item = blockIdx.x;
+    if (item < p.num_items) store_idx(load_idx(item));
+    for (; item < p.num_items; item += gridDim.x) {
+      named_bar_sync(1, kProducers);  // idx_s holds this group's indices
+      const int64_t g = item / p.co_blocks;
+      const int cb = static_cast<int>(item - g * p.co_blocks);
+      const int64_t next = item + gridDim.x;
+      const int nact_next = next < p.num_items ? load_idx(next) : 0;
+      uint32_t mask = group_mask(g);
+      for (int j = 0; mask; ++j) {
         const int v = __ffs(mask) - 1;
         mask &= mask - 1;
-        const int4 idx = __ldg(reinterpret_cast<const int4*>(p.gidx + (t * p.K + v) * 128) + lane);
+        int rows_idx[TPI][CPR];
+#pragma unroll
+        for (int i = 0; i < TPI; ++i)
+#pragma unroll
+          for (int c = 0; c < CPR; ++c) rows_idx[i][c] = idx_s[(j * TPI + i) * 128 + row0 + c * RSTEP];
         for (int kc = 0; kc < p.nchunks; ++kc) {
-          int w = 1;
-          if (lane == 0) w = mbar_wait(empty0 + 8u * stage, phase ^ 1u, p.err) ? 1 : 0;
+          abort = abort || (*reinterpret_cast<volatile int*>(s_tmem + 1) != 0);
+          int w = 0;
+          if (lane == 0 && !abort) w = mbar_wait(empty0 + 8u * stage, phase ^ 1u, p.err) ? 1 : 0;
           w = __shfl_sync(0xffffffffu, w, 0);
           if (!w) {
-            ok = false;
-            break;
+            if (!abort && lane == 0) *reinterpret_cast<volatile int*>(s_tmem + 1) = 1;
+            abort = true;
+            continue;
           }
-          if (lane == 0) mbar_arrive_expect_tx(full0 + 8u * stage, stage_tx);
-          __syncwarp();
           const uint32_t sbase = smem_base + static_cast<uint32_t>(stage * S::kStageBytes);
-          tma_gather4(sbase + static_cast<uint32_t>(lane * 4 * KC * 2), &tmA, kc * KC, idx.x, idx.y, idx.z, idx.w,
-                      full0 + 8u * stage);
-          if (lane == 0) tma_load_2d(sbase + S::kABytes, &tmB, v * p.ci + kc * KC, cb * bn, full0 + 8u * stage);
-          used |= 1u << stage;
-          used_par = (used_par & ~(1u << stage)) | (phase << stage);
+          if (pt == 0) {
+            mbar_arrive_expect_tx(full0 + 8u * stage, b_tx);
+            tma_load_2d(sbase + TPI * S::kABytes, &tmB, v * p.ci + kc * KC, cb * bn, full0 + 8u * stage);
+            used |= 1u << stage;
+            used_par = (used_par & ~(1u << stage)) | (phase << stage);
+          }
+#pragma unroll
+          for (int i = 0; i < TPI; ++i) {
+#pragma unroll
+            for (int c = 0; c < CPR; ++c) {
+              const int r = row0 + c * RSTEP;
+              const int src_row = rows_idx[i][c];
+              const uint32_t o = static_cast<uint32_t>(r * ROWB + chunk * 16);
+              const uint32_t sw = o ^ (((o >> 7) & static_cast<uint32_t>(CPR - 1)) << 4);
+              const T* src =
+                  src_row >= 0 ? feats + static_cast<int64_t>(src_row) * p.ci + kc * KC + chunk * 8 : feats;
+              cp_async16(sbase + i * S::kABytes + sw, src, src_row >= 0 ? 16u : 0u);
+            }
+          }
+          cp_async_arrive_noinc(full0 + 8u * stage);
           if (++stage == S::kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
+      if (next < p.num_items) {
+        named_bar_sync(1, kProducers);  // every producer has read this group's indices
+        store_idx(nact_next);
+      }
     }
-    if (!ok && lane == 0) {
-      // Error exit: let copies already issued into our shared memory land.
+    cp_async_wait_all();
+    if (abort && pt == 0) {
+      // Error exit: let weight copies already issued into our shared memory land.
       for (int s = 0; s < S::kStages; ++s)
         if (used & (1u << s)) mbar_wait(full0 + 8u * s, (used_par >> s) & 1u, nullptr);
     }
-    __syncwarp();
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(128, bn, BF16);
@@ -256,24 +381,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t phase = 0, it = 0;
       bool ok = true;
       for (int64_t item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++it) {
-        const int64_t t = item / p.co_blocks;
+        const int64_t g = item / p.co_blocks;
         const uint32_t acc = it & 1u, aph = (it >> 1) & 1u;
         if (!mbar_wait(tempty0 + 8u * acc, aph ^ 1u, p.err)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * static_cast<uint32_t>(BNMAX);
-        const int nsteps = __popc(__ldg(p.tile_mask + t)) * p.nchunks;
+        const uint32_t d_tmem = tmem_base + acc * static_cast<uint32_t>(S::kAccCols);
+        const int nsteps = __popc(group_mask(g)) * p.nchunks;
         for (int s = 0; s < nsteps; ++s) {
           if (!mbar_wait(full0 + 8u * stage, phase, p.err)) {
             ok = false;
             break;
           }
+          // The rows were written by cp.async and signalled through
+          // cp.async.mbarrier.arrive; like CUTLASS's sm100 cp.async mainloop,
+          // no extra proxy fence is placed here (a consumer-side
+          // fence.proxy.async serialises the pipeline on all in-flight copies).
           tc_fence_after();
           const uint32_t a0 = smem_base + static_cast<uint32_t>(stage * S::kStageBytes);
-          const uint32_t b0 = a0 + S::kABytes;
+          const uint32_t b0 = a0 + TPI * S::kABytes;
 #pragma unroll
-          for (int k = 0; k < KC / 16; ++k) {
-            tc_mma_f16(d_tmem, smem_desc(a0 + 32u * k, Z::kSbo, Z::kMode), smem_desc(b0 + 32u * k, Z::kSbo, Z::kMode),
-                       idesc, (s > 0 || k > 0) ? 1u : 0u);
+          for (int i = 0; i < TPI; ++i) {
+#pragma unroll
+            for (int k = 0; k < KC / 16; ++k) {
+              tc_mma_f16(d_tmem + i * BNMAX, smem_desc(a0 + i * S::kABytes + 32u * k, Z::kSbo, Z::kMode),
+                         smem_desc(b0 + 32u * k, Z::kSbo, Z::kMode), idesc, (s > 0 || k > 0) ? 1u : 0u);
+            }
           }
           tc_commit(empty0 + 8u * stage);
           if (++stage == S::kStages) {
@@ -296,41 +428,49 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const T* bias = static_cast<const T*>(p.bias);
     const T* res = static_cast<const T*>(p.residual);
     T* out = static_cast<T*>(p.out);
+    uint8_t* wbuf = out_s + (warp - (kMmaWarp + 1)) * (32 * 64);
     uint32_t it = 0;
     for (int64_t item = blockIdx.x; item < p.num_items; item += gridDim.x, ++it) {
-      const int64_t t = item / p.co_blocks;
-      const int cb = static_cast<int>(item - t * p.co_blocks);
+      const int64_t g = item / p.co_blocks;
+      const int cb = static_cast<int>(item - g * p.co_blocks);
       const uint32_t acc = it & 1u, aph = (it >> 1) & 1u;
       int w = 1;
       if (lane == 0) w = mbar_wait(tfull0 + 8u * acc, aph, p.err) ? 1 : 0;
       w = __shfl_sync(0xffffffffu, w, 0);
       if (!w) break;
       tc_fence_after();
-      const int r = __ldg(p.tile_rows + t * 128 + row);
-      const bool live = __ldg(p.tile_mask + t) != 0u;
-      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * static_cast<uint32_t>(BNMAX);
+      const bool live = group_mask(g) != 0u;
       const int col0 = cb * bn;
       const int bn32 = bn & ~31;  // columns handled 32 at a time; a 16-wide tail follows when bn % 32 == 16
-      float mean = 0.f, rstd = 1.f;
-      if (p.epi & SC_EPI_LAYERNORM) {
-        float s1 = 0.f;
-        for (int c0 = 0; c0 < bn32; c0 += 32) s1 += chunk_sum<T, 32>(tb, c0, live, bias, col0, 0.f, false);
-        if (bn32 < bn) s1 += chunk_sum<T, 16>(tb, bn32, live, bias, col0, 0.f, false);
-        mean = s1 / static_cast<float>(bn);
-        float s2 = 0.f;
-        for (int c0 = 0; c0 < bn32; c0 += 32) s2 += chunk_sum<T, 32>(tb, c0, live, bias, col0, mean, true);
-        if (bn32 < bn) s2 += chunk_sum<T, 16>(tb, bn32, live, bias, col0, mean, true);
-        rstd = rsqrtf(s2 / static_cast<float>(bn) + p.eps);
+#pragma unroll 1
+      for (int i = 0; i < TPI; ++i) {
+        const int64_t t = g * TPI + i;
+        const int r = t < p.num_tiles ? __ldg(p.tile_rows + t * 128 + row) : -1;
+        const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                            acc * static_cast<uint32_t>(S::kAccCols) + static_cast<uint32_t>(i * BNMAX);
+        float mean = 0.f, rstd = 1.f;
+        if (p.epi & SC_EPI_LAYERNORM) {
+          float s1 = 0.f;
+          for (int c0 = 0; c0 < bn32; c0 += 32) s1 += chunk_sum<T, 32>(tb, c0, live, bias, col0, 0.f, false);
+          if (bn32 < bn) s1 += chunk_sum<T, 16>(tb, bn32, live, bias, col0, 0.f, false);
+          mean = s1 / static_cast<float>(bn);
+          float s2 = 0.f;
+          for (int c0 = 0; c0 < bn32; c0 += 32) s2 += chunk_sum<T, 32>(tb, c0, live, bias, col0, mean, true);
+          if (bn32 < bn) s2 += chunk_sum<T, 16>(tb, bn32, live, bias, col0, mean, true);
+          rstd = rsqrtf(s2 / static_cast<float>(bn) + p.eps);
+        }
+        for (int c0 = 0; c0 < bn32; c0 += 32)
+          epi_chunk<T, 32>(tb, c0, live, bias, res, out, r, p.co, col0, mean, rstd, p.epi, wbuf, lane);
+        if (bn32 < bn) epi_chunk<T, 16>(tb, bn32, live, bias, res, out, r, p.co, col0, mean, rstd, p.epi, wbuf, lane);
       }
-      for (int c0 = 0; c0 < bn32; c0 += 32) epi_chunk<T, 32>(tb, c0, live, bias, res, out, r, p.co, col0, mean, rstd, p.epi);
-      if (bn32 < bn) epi_chunk<T, 16>(tb, bn32, live, bias, res, out, r, p.co, col0, mean, rstd, p.epi);
       tc_fence_before();
       mbar_arrive(tempty0 + 8u * acc);
+      __syncwarp();
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, S::kTmemCols);
   }
@@ -368,29 +508,33 @@ bool make_map_2d(CUtensorMap* m, bool bf16, const void* base, uint64_t inner, ui
              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int KC, int BNMAX, bool BF16>
+template <int KC, int BNMAX, int TPI, bool BF16>
 sc_status launch_tc(Handle* h, const KMap* km, const void* feats, const void* weight, TcParams p) {
-  using S = TcShape<KC, BNMAX>;
+  using S = TcShape<KC, BNMAX, TPI>;
   using Z = SwizzleCfg<KC>;
-  CUtensorMap ta, tb;
-  if (!make_map_2d(&ta, BF16, feats, p.ci, km->n_in, static_cast<uint64_t>(p.ci) * 2, KC, 1, Z::kTma) ||
-      !make_map_2d(&tb, BF16, weight, static_cast<uint64_t>(km->K) * p.ci, p.co,
+  CUtensorMap tb;
+  p.feats = feats;
+  if (!make_map_2d(&tb, BF16, weight, static_cast<uint64_t>(km->K) * p.ci, p.co,
                    static_cast<uint64_t>(km->K) * p.ci * 2, KC, p.bn, Z::kTma))
     return set_error(h, SC_ECUDA, "cuTensorMapEncodeTiled failed");
-  auto kern = conv_tc_kernel<KC, BNMAX, BF16>;
+  p.num_items = ((p.num_tiles + TPI - 1) / TPI) * p.co_blocks;
+  auto kern = conv_tc_kernel<KC, BNMAX, TPI, BF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
   if (e != cudaSuccess) return cuda_error(h, e, "conv smem attribute");
   const int64_t grid = std::min<int64_t>(p.num_items, h->num_sms);
-  kern<<<static_cast<unsigned>(grid), kTcThreads, S::kSmemBytes, h->stream>>>(ta, tb, p);
+  ++h->launches;
+  kern<<<static_cast<unsigned>(grid), kTcThreads, S::kSmemBytes, h->stream>>>(tb, p);
   e = cudaGetLastError();
   return e == cudaSuccess ? SC_OK : cuda_error(h, e, "conv launch");
 }
 
 template <int KC, bool BF16>
 sc_status dispatch_bn(Handle* h, const KMap* km, const void* feats, const void* weight, const TcParams& p) {
-  if (p.bn <= 64) return launch_tc<KC, 64, BF16>(h, km, feats, weight, p);
-  if (p.bn <= 128) return launch_tc<KC, 128, BF16>(h, km, feats, weight, p);
-  return launch_tc<KC, 256, BF16>(h, km, feats, weight, p);
+  // Up to 128 output channels two tiles share each weight stage; wider
+  // outputs already reuse each gathered row across 256 MMA columns.
+  if (p.bn <= 64) return launch_tc<KC, 64, 2, BF16>(h, km, feats, weight, p);
+  if (p.bn <= 128) return launch_tc<KC, 128, 2, BF16>(h, km, feats, weight, p);
+  return launch_tc<KC, 256, 1, BF16>(h, km, feats, weight, p);
 }
 
 template <bool BF16>
@@ -429,6 +573,7 @@ sc_status check_gather_bounds(Handle* h, const KMap* km) {
   int herr = 0;
   e = cudaMemsetAsync(derr, 0, 16, h->stream);
   if (e == cudaSuccess) {
+    ++h->launches;
     k_check_gidx<<<static_cast<unsigned>((total + 255) / 256), 256, 0, h->stream>>>(km->gidx, total, km->n_in, derr);
     e = cudaMemcpyAsync(&herr, derr, 4, cudaMemcpyDeviceToHost, h->stream);
   }
@@ -469,6 +614,7 @@ sc_status conv_tc(Handle* h, const KMap* km, const void* feats, const void* weig
   p.residual = residual;
   p.out = out;
   p.co_blocks = co / bn;
+  p.num_tiles = km->num_tiles;
   p.num_items = km->num_tiles * p.co_blocks;
   p.K = km->K;
   p.ci = ci;

@@ -17,6 +17,7 @@ struct Handle {
   cudaStream_t stream = nullptr;
   int num_sms = 148;
   int* derr = nullptr;  // device error word written by conv kernels
+  unsigned long long launches = 0;  // kernels this handle has launched
   std::string last_error;
 };
 

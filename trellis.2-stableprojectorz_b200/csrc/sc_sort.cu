@@ -197,12 +197,14 @@ sc_status radix_sort_impl(Handle* h, K* keys, uint32_t* vals, K* keys_alt, uint3
   cudaError_t e = cudaMemsetAsync(temp, 0, need, h->stream);
   if (e != cudaSuccess) return cuda_error(h, e, "radix sort memset");
   const int hgrid = static_cast<int>(std::min<int64_t>(ntiles, static_cast<int64_t>(h->num_sms) * 4));
+  ++h->launches;
   rs_hist_kernel<K><<<hgrid, kRsThreads, 0, h->stream>>>(keys, n, begin_bit, end_bit, passes, ghist);
   K* ksrc = keys;
   K* kdst = keys_alt;
   uint32_t* vsrc = vals;
   uint32_t* vdst = vals_alt;
   for (int p = 0; p < passes; ++p) {
+    ++h->launches;
     rs_onesweep_kernel<K><<<static_cast<unsigned>(ntiles), kRsThreads, 0, h->stream>>>(
         ksrc, vsrc, kdst, vdst, n, begin_bit + 8 * p, end_bit, ghist + p * kRsBins,
         status + static_cast<size_t>(p) * ntiles * kRsBins, counters + p, err);

@@ -67,6 +67,10 @@ class Engine:
     def check(self, status, what=""):
         L.check(status, self.handle, what)
 
+    def launch_count(self):
+        """Kernels launched through this handle so far."""
+        return int(self.lib.sc_launch_count(self.handle))
+
     def synchronize(self):
         self.check(self.lib.sc_synchronize(self.handle), "synchronize")
 
@@ -94,15 +98,17 @@ def get_engine(device=None, map_mode="hash"):
 class KernelMap:
     """A built neighbour / gather map (``sc_kmap*``), freed with the object."""
 
-    def __init__(self, engine, ptr, kind, keepalive=None):
+    def __init__(self, engine, ptr, kind, n_in=None, n_out=None, kernel_volume=None, keepalive=None):
         self.engine = engine
         self.ptr = ptr
         self.kind = kind
         self._keepalive = keepalive
-        info = self.info()
-        self.n_in = info["n_in"]
-        self.n_out = info["n_out"]
-        self.kernel_volume = info["kernel_volume"]
+        if n_in is None or n_out is None or kernel_volume is None:
+            info = self.info()  # waits for the build
+            n_in, n_out, kernel_volume = info["n_in"], info["n_out"], info["kernel_volume"]
+        self.n_in = int(n_in)
+        self.n_out = int(n_out)
+        self.kernel_volume = int(kernel_volume)
 
     def info(self):
         inf = L.ScKmapInfo()
@@ -162,7 +168,8 @@ def build_kmap(coords, dilation=1, engine=None, tile_sort=True, check=True):
     p = ctypes.c_void_p()
     eng.check(eng.lib.sc_kmap_build(eng.handle, _ptr(coords), coords.shape[0], 3, int(dilation),
                                     _flags(tile_sort, check), ctypes.byref(p)), "sc_kmap_build")
-    return KernelMap(eng, p, L.SC_KMAP_SUBM)
+    n = coords.shape[0]
+    return KernelMap(eng, p, L.SC_KMAP_SUBM, n, n, 27)
 
 
 def build_down2(coords, engine=None, tile_sort=True):
@@ -183,7 +190,7 @@ def build_up2(down, tile_sort=True):
     p = ctypes.c_void_p()
     eng.check(eng.lib.sc_kmap_build_up2(eng.handle, down.ptr, _flags(tile_sort, True), ctypes.byref(p)),
               "sc_kmap_build_up2")
-    return KernelMap(eng, p, L.SC_KMAP_UP2, keepalive=down)
+    return KernelMap(eng, p, L.SC_KMAP_UP2, down.n_out, down.n_in, 8, keepalive=down)
 
 
 def conv3d(kmap, feats, weight, bias=None, residual=None, silu=False, layernorm=False, eps=1e-6, out=None):

@@ -165,7 +165,7 @@ def _normal(rng, shape, var):
 
 def _c1(rng, scale):
     grid = 64
-    axes = rng.uniform(18, 30, 3)
+    axes = rng.uniform(18 * scale, 30 * scale, 3)
     vox = ellipsoid_shell((32, 32, 32), axes, 1.0, grid)
     coords = _finish(_union([vox], 0))
     ci = co = 64
