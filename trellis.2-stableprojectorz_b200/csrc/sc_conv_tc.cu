@@ -236,7 +236,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_init(tempty0, 128);
     mbar_init(tempty0 + 8u, 128);
     mbar_init(done_bar, 1);
-    s_tmem[1] = 0;  // producer abort flag
     fence_mbar_init();
     prefetch_tmap(&tmB);
   }
@@ -272,9 +271,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     uint32_t used = 0, used_par = 0;  // stages whose weight TMA was issued, parity of the last issue
-    // A timed-out wait sets `abort`; producers then keep walking the same
-    // item sequence without waiting or copying, so the named barrier below is
-    // reached the same number of times by all four warps.
+    // A timed-out wait sets this warp's `abort`; the warp then keeps walking
+    // the same item sequence without waiting or copying, so the named barrier
+    // below is reached the same number of times by all four warps (the other
+    // warps time out on their own waits).  No shared-memory flag is polled:
+    // a shared load issued after this thread's cp.async waits for those
+    // copies to land and would serialise the pipeline.
     bool abort = false;
     // gather-index prefetch: warp w loads active offsets j = w, w+4, ... (<= 7 each)
     int4 pre[7][TPI];
@@ -326,12 +328,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int c = 0; c < CPR; ++c) rows_idx[i][c] = idx_s[(j * TPI + i) * 128 + row0 + c * RSTEP];
         for (int kc = 0; kc < p.nchunks; ++kc) {
-          abort = abort || (*reinterpret_cast<volatile int*>(s_tmem + 1) != 0);
           int w = 0;
           if (lane == 0 && !abort) w = mbar_wait(empty0 + 8u * stage, phase ^ 1u, p.err) ? 1 : 0;
-          w = __shfl_sync(0xffffffffu, w, 0);
-          if (!w) {
-            if (!abort && lane == 0) *reinterpret_cast<volatile int*>(s_tmem + 1) = 1;
+          if (!__all_sync(0xffffffffu, lane != 0 || w != 0)) {
             abort = true;
             continue;
           }

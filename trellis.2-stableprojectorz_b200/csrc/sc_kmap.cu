@@ -44,16 +44,33 @@ __device__ __forceinline__ uint32_t mix64(unsigned long long k) {
 // Batch index in [0, 32767] keeps the top key bit clear, so the all-ones
 // empty-slot key can never collide with a voxel key.
 // Probe sequence of a voxel key.  Probe 0 is the home slot: the 4x4x4 block
-// containing the voxel owns a 64-slot region (hash of the block key) and the
-// voxel's position inside the block picks the slot, so the 27 neighbours of a
-// voxel start in at most eight nearby regions (cache-local).  Probe i >= 1 is
-// a fresh hash of (key, i): collisions leave the region instead of walking
-// along it, which keeps chains as short as with a fully random hash
+// containing the voxel owns a 64-slot region (hash of the block coordinates)
+// and the voxel's position inside the block picks the slot, so the 27
+// neighbours of a voxel start in at most eight nearby regions (cache-local).
+// Probe i >= 1 is a fresh hash of (key, i): collisions leave the region instead
+// of walking along it, which keeps chains as short as with a fully random hash
 // (at load <= 1/4: mean 1.2 probes, p99 3 on the 256^3 shell workload).
+//
+// The block hash is separable: per-axis terms are multiplied by odd constants
+// and xored, then finalised with a 32-bit multiply-xorshift, so a voxel's 27
+// neighbours need only 3 terms per axis plus one finaliser each.
+__device__ __forceinline__ uint32_t axis_term(int v, uint32_t mul) { return static_cast<uint32_t>(v) * mul; }
+constexpr uint32_t kMulB = 0x27D4EB2Fu, kMulX = 0x9E3779B1u, kMulY = 0x85EBCA77u, kMulZ = 0xC2B2AE3Du;
+__device__ __forceinline__ uint32_t fin32(uint32_t h) {
+  h ^= h >> 15;
+  h *= 0x2C1B3C6Du;
+  h ^= h >> 12;
+  h *= 0x297A2D39u;
+  h ^= h >> 15;
+  return h;
+}
+__device__ __forceinline__ uint32_t local_slot(int x, int y, int z) {
+  return static_cast<uint32_t>(((x & 3) << 4) | ((y & 3) << 2) | (z & 3));
+}
 __device__ __forceinline__ uint32_t home_slot(int b, int x, int y, int z, uint32_t cap_mask) {
-  const unsigned long long blk = pack16(b, x >> 2, y >> 2, z >> 2);
-  const uint32_t local = static_cast<uint32_t>(((x & 3) << 4) | ((y & 3) << 2) | (z & 3));
-  return ((mix64(blk) << 6) | local) & cap_mask;
+  const uint32_t h = fin32(axis_term(b, kMulB) ^ axis_term(x >> 2, kMulX) ^ axis_term(y >> 2, kMulY) ^
+                           axis_term(z >> 2, kMulZ));
+  return ((h << 6) | local_slot(x, y, z)) & cap_mask;
 }
 __device__ __forceinline__ uint32_t rehash_slot(unsigned long long key, uint32_t i, uint32_t cap_mask) {
   return mix64(key ^ (static_cast<unsigned long long>(i) * 0x9E3779B97F4A7C15ull)) & cap_mask;
@@ -114,10 +131,12 @@ __device__ __forceinline__ void write_rows_and_count(const int32_t* s_map, int64
 }
 
 // One thread per output voxel.  The 26 non-centre neighbours are probed in
-// three groups of nine (one per dx); within a group all pending probes advance
-// one slot per round, so a thread waits for the longest chain of the group
-// rather than the sum of all chains.  The row is staged in shared memory so the
-// [N,27] map is written with coalesced stores.
+// two groups of thirteen; within a group all pending probes advance one step
+// per round, so a thread waits for the longest chain of the group rather than
+// the sum of all chains.  Neighbour keys are the voxel's packed key plus packed
+// offsets, and home slots come from per-axis hash terms computed once.  The row
+// is staged in shared memory so the [N,27] map is written with coalesced
+// stores.
 __global__ void __launch_bounds__(128) k_probe_hash(const int4* __restrict__ coords, int64_t n,
                                                     const Slot* __restrict__ slots, uint32_t cap_mask, int dil,
                                                     int32_t* __restrict__ map, uint32_t* __restrict__ row_mask,
@@ -125,37 +144,57 @@ __global__ void __launch_bounds__(128) k_probe_hash(const int4* __restrict__ coo
   __shared__ int32_t s_map[128 * 27];
   const int64_t row0 = blockIdx.x * 128ll;
   const int64_t i = row0 + threadIdx.x;
+  int32_t* my = s_map + threadIdx.x * 27;
   uint32_t m = 0;
   if (i < n) {
     const int4 c = coords[i];
     const bool cok = coord_ok(c);
+    const unsigned long long base = pack16(c.x, c.y, c.z, c.w);
+    const uint32_t hb = axis_term(c.x, kMulB);
+    uint32_t hx[3], hy[3], hz[3], lx[3], ly[3], lz[3];
+    bool vx[3], vy[3], vz[3];
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+      const int d = (a - 1) * dil;
+      const int x = c.y + d, y = c.z + d, z = c.w + d;
+      vx[a] = cok && static_cast<unsigned>(x) <= 65535u;
+      vy[a] = cok && static_cast<unsigned>(y) <= 65535u;
+      vz[a] = cok && static_cast<unsigned>(z) <= 65535u;
+      hx[a] = axis_term(x >> 2, kMulX);
+      hy[a] = axis_term(y >> 2, kMulY);
+      hz[a] = axis_term(z >> 2, kMulZ);
+      lx[a] = static_cast<uint32_t>(x & 3) << 4;
+      ly[a] = static_cast<uint32_t>(y & 3) << 2;
+      lz[a] = static_cast<uint32_t>(z & 3);
+    }
     const ulonglong2* sl = reinterpret_cast<const ulonglong2*>(slots);
-#pragma unroll 1
-    for (int g = 0; g < 3; ++g) {
-      const int x = c.y + (g - 1) * dil;
-      uint32_t pos[9];
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      uint32_t pos[13];
       uint32_t pend = 0;
 #pragma unroll
-      for (int k = 0; k < 9; ++k) {
-        const int y = c.z + (k / 3 - 1) * dil, z = c.w + (k % 3 - 1) * dil;
-        const bool inb = cok && static_cast<unsigned>(x) <= 65535u && static_cast<unsigned>(y) <= 65535u &&
-                         static_cast<unsigned>(z) <= 65535u;
-        pos[k] = inb ? home_slot(c.x, x, y, z, cap_mask) : 0u;
-        if (inb && !(g == 1 && k == 4)) pend |= 1u << k;
-        s_map[threadIdx.x * 27 + g * 9 + k] = (g == 1 && k == 4) ? static_cast<int>(i) : -1;
+      for (int k = 0; k < 13; ++k) {
+        const int v = g * 14 + k;  // 0..12, then 14..26
+        const int a = v / 9, bb = (v / 3) % 3, cc = v % 3;
+        const bool inb = vx[a] && vy[bb] && vz[cc];
+        pos[k] = ((fin32(hb ^ hx[a] ^ hy[bb] ^ hz[cc]) << 6) | lx[a] | ly[bb] | lz[cc]) & cap_mask;
+        if (inb) pend |= 1u << k;
+        my[v] = -1;
       }
       for (uint32_t round = 0; pend && round <= cap_mask; ++round) {
-        ulonglong2 sv[9];
+        ulonglong2 sv[13];
 #pragma unroll
-        for (int k = 0; k < 9; ++k)
+        for (int k = 0; k < 13; ++k)
           if (pend & (1u << k)) sv[k] = __ldg(sl + pos[k]);
 #pragma unroll
-        for (int k = 0; k < 9; ++k) {
+        for (int k = 0; k < 13; ++k) {
           if (!(pend & (1u << k))) continue;
-          const int y = c.z + (k / 3 - 1) * dil, z = c.w + (k % 3 - 1) * dil;
-          const unsigned long long q = pack16(c.x, x, y, z);
+          const int v = g * 14 + k;
+          const long long dq = (static_cast<long long>(v / 9 - 1) << 32) + (static_cast<long long>((v / 3) % 3 - 1) << 16) +
+                               static_cast<long long>(v % 3 - 1);
+          const unsigned long long q = base + static_cast<unsigned long long>(dq * dil);
           if (sv[k].x == q) {
-            s_map[threadIdx.x * 27 + g * 9 + k] = static_cast<int>(static_cast<uint32_t>(sv[k].y));
+            my[v] = static_cast<int>(static_cast<uint32_t>(sv[k].y));
             pend &= ~(1u << k);
           } else if (sv[k].x == kEmptyKey) {
             pend &= ~(1u << k);
@@ -165,8 +204,9 @@ __global__ void __launch_bounds__(128) k_probe_hash(const int4* __restrict__ coo
         }
       }
     }
+    my[13] = static_cast<int>(i);
 #pragma unroll
-    for (int v = 0; v < 27; ++v) m |= (s_map[threadIdx.x * 27 + v] >= 0 ? 1u : 0u) << v;
+    for (int v = 0; v < 27; ++v) m |= (my[v] >= 0 ? 1u : 0u) << v;
     row_mask[i] = m;
   }
   write_rows_and_count(s_map, row0, n, 27, map, m, counters);
