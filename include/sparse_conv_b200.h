@@ -133,6 +133,20 @@ SC_API sc_status sc_kmap_build_up2(sc_handle* h, const sc_kmap* down, uint32_t f
 /* Parent coords of a down-sample map: int32 [n_out, 4]. */
 SC_API sc_status sc_kmap_out_coords(sc_handle* h, const sc_kmap* km, int32_t* coords_out);
 
+/* Submanifold 3x3x3 neighbour map written straight into `map_out`
+ * (int32 [n, 27], caller-owned device memory) without allocating any device
+ * memory.  No counterpart in the reference.  For callers that must not let a
+ * library allocate device memory (a host runtime that budgets all device
+ * memory itself, or a latency-sensitive path that cannot wait on an allocator).
+ * Scratch is a fixed 8 MiB __device__ array held by every GPU that loads the
+ * library: n must be <= SC_NOALLOC_MAX_VOXELS (else SC_EINVAL).  Calls share
+ * that scratch, so calls that overlap on the GPU race; order them.  The first
+ * call on a device looks up the scratch address; make it before any stream
+ * capture on that device.  Waits for the build and returns its status. */
+#define SC_NOALLOC_MAX_VOXELS 131072
+SC_API sc_status sc_kmap_build_noalloc(sc_handle* h, const int32_t* coords, int64_t n, int32_t dilation,
+                                       int32_t* map_out);
+
 /* Writes the canonical int32 [n_out, K] map (for bit-exact checks). */
 SC_API sc_status sc_kmap_export(sc_handle* h, const sc_kmap* km, int32_t* map_out);
 

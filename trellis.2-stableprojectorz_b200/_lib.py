@@ -28,6 +28,7 @@ SC_MAP_HASH, SC_MAP_SORT = 0, 1
 SC_KMAP_SUBM, SC_KMAP_DOWN2, SC_KMAP_UP2 = 0, 1, 2
 SC_BUILD_NO_TILE_SORT, SC_BUILD_DEFER_CHECK = 1, 2
 SC_EPI_SILU, SC_EPI_RESIDUAL, SC_EPI_LAYERNORM = 1, 2, 4
+SC_NOALLOC_MAX_VOXELS = 131072
 
 
 class SparseConvError(RuntimeError):
@@ -76,6 +77,7 @@ _SIGNATURES = {
     "sc_kmap_build": (_I32, [_P, _P, _I64, _I32, _I32, _U32, _PP]),
     "sc_kmap_build_down2": (_I32, [_P, _P, _I64, _U32, _PP]),
     "sc_kmap_build_up2": (_I32, [_P, _P, _U32, _PP]),
+    "sc_kmap_build_noalloc": (_I32, [_P, _P, _I64, _I32, _P]),
     "sc_kmap_out_coords": (_I32, [_P, _P, _P]),
     "sc_kmap_export": (_I32, [_P, _P, _P]),
     "sc_kmap_get_info": (_I32, [_P, _P, ctypes.POINTER(ScKmapInfo)]),

@@ -224,6 +224,18 @@ sc_status sc_kmap_build_up2(sc_handle* h, const sc_kmap* down, uint32_t flags, s
   return wrap_kmap(H, km, flags, out);
 }
 
+sc_status sc_kmap_build_noalloc(sc_handle* h, const int32_t* coords, int64_t n, int32_t dilation,
+                                int32_t* map_out) {
+  if (!h) return SC_EINVAL;
+  Handle* H = &h->impl;
+  if (n < 0) return sc::set_error(H, SC_EINVAL, "n must be >= 0");
+  if (n > 0 && (!coords || !sc::aligned(coords, 16) || !map_out || !sc::aligned(map_out, 4)))
+    return sc::set_error(H, SC_EINVAL, "coords (16-byte aligned) and map_out must be device pointers");
+  if (dilation < 1 || dilation > 1024) return sc::set_error(H, SC_EINVAL, "dilation must be in [1, 1024]");
+  sc::DeviceGuard g(H->device);
+  return sc::build_subm_noalloc(H, coords, n, dilation, map_out);
+}
+
 sc_status sc_kmap_out_coords(sc_handle* h, const sc_kmap* km, int32_t* coords_out) {
   if (!h || !km) return SC_EINVAL;
   Handle* H = &h->impl;

@@ -53,6 +53,8 @@ sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int dilation, 
 sc_status build_down2(Handle* h, const int32_t* coords, int64_t n, uint32_t flags, KMap** out);
 sc_status build_up2(Handle* h, const KMap* down, uint32_t flags, KMap** out);
 sc_status export_map(Handle* h, const KMap* km, int32_t* map_out);
+// allocation-free map build into caller memory (sc_noalloc.cu)
+sc_status build_subm_noalloc(Handle* h, const int32_t* coords, int64_t n, int dilation, int32_t* map_out);
 void free_kmap(Handle* h, KMap* km);
 
 // conv launchers
