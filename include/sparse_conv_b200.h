@@ -119,6 +119,13 @@ SC_API uint64_t sc_launch_count(const sc_handle* h);
 SC_API sc_status sc_kmap_build(sc_handle* h, const int32_t* coords, int64_t n, int32_t kernel_size, int32_t dilation,
                         uint32_t flags, sc_kmap** out);
 
+/* As sc_kmap_build, but only the first n_out rows of `coords` are outputs;
+ * neighbours are looked up among all n_in rows.  Used by sharded convs: a
+ * rank's owned voxels come first, its halo voxels (neighbours owned by other
+ * ranks) after them.  Replaces the same passes as sc_kmap_build. */
+SC_API sc_status sc_kmap_build_ex(sc_handle* h, const int32_t* coords, int64_t n_in, int64_t n_out,
+                                  int32_t kernel_size, int32_t dilation, uint32_t flags, sc_kmap** out);
+
 /* Stride-2 2x2x2 down-sample map: parents are the unique (b, x>>1, y>>1, z>>1)
  * in ascending lexicographic order; map column = (x&1)*4 + (y&1)*2 + (z&1).
  * Replaces the stride-2 sparse conv of trellis2/modules/sparse/conv (absent

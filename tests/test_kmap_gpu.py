@@ -149,3 +149,17 @@ def test_map_build_is_deterministic(pkg, cuda):
     a = pkg.build_kmap(c)
     b = pkg.build_kmap(c)
     assert torch.equal(a.export(), b.export())
+
+
+def test_map_with_fewer_outputs(pkg, oracle, cuda):
+    # outputs are the first n_out rows, neighbours come from all rows (sharded convs)
+    w = pkg.workloads.make_workload(3, scale=0.3)
+    perm = pkg.workloads.shuffle_rows(w.n, 3)
+    coords = np.ascontiguousarray(w.coords[perm])
+    ref = oracle.kmap_sorted(coords, w.spatial_shape)
+    c = torch.from_numpy(coords).to(cuda)
+    for n_out in (0, 1, 777, w.n // 2, w.n):
+        for mode in ("hash", "sort"):
+            km = pkg.build_kmap(c, n_out=n_out, engine=pkg.get_engine(cuda, mode))
+            assert km.n_out == n_out and km.n_in == w.n
+            assert np.array_equal(km.export().cpu().numpy(), ref[:n_out]), (n_out, mode)

@@ -78,9 +78,10 @@ struct TcShape {
   static constexpr int kABytes = 128 * KC * 2;  // one tile's A operand
   static constexpr int kBBytes = BNMAX * KC * 2;
   static constexpr int kStageBytes = TPI * kABytes + kBBytes;
-  static constexpr int kOutBytes = 4 * 32 * 32 * 2;  // epilogue staging: per warp 32 rows x 32 columns
+  static constexpr int kOutBytes = 4 * 32 * 16 * 2;  // epilogue staging: per warp 32 rows x 16 columns
   static constexpr int kIdxBytes = 27 * 128 * TPI * 4;  // gather indices of the tile group being produced
-  static constexpr int kStageBudget = 224 * 1024 - kIdxBytes - kOutBytes - 2048;
+  static constexpr int kBarBytesPlan = 256, kAlignSlack = 1024;
+  static constexpr int kStageBudget = 227 * 1024 - kIdxBytes - kOutBytes - kBarBytesPlan - kAlignSlack;
   static constexpr int kStagesFit = kStageBudget / kStageBytes;
   static constexpr int kStages = kStagesFit > 12 ? 12 : kStagesFit;
   static_assert(kStages >= 2, "not enough shared memory for two stages");
@@ -153,10 +154,9 @@ __device__ __forceinline__ float chunk_sum(uint32_t tb, int c0, bool live, const
 }
 
 // Epilogue of W columns (32 or 16) of the warp's 32 output rows: +bias,
-// LayerNorm, SiLU, +residual, bf16/f16 pack.  Each lane stages its row
-// segment in the warp's shared-memory buffer (16-byte chunks XOR-swizzled by
-// row pair, conflict-free), then the warp writes the segments back with each store instruction
-// covering whole row segments of several rows, not 16 bytes of 32 rows.
+// LayerNorm, SiLU, +residual, bf16/f16 pack, then a store through the warp's
+// shared-memory buffer so each store instruction covers whole 32-byte row
+// segments of 16 rows instead of 16 bytes of 32 rows.
 template <typename T, int W>
 __device__ __forceinline__ void epi_chunk(uint32_t tb, int c0, bool live, const T* bias, const T* res, T* out,
                                           int r, int co, int col0, float mean, float rstd, uint32_t epi,
@@ -176,33 +176,39 @@ __device__ __forceinline__ void epi_chunk(uint32_t tb, int c0, bool live, const 
 #pragma unroll
     for (int j = 0; j < W; ++j) v[j] += rr[j];
   }
-  constexpr int CH = W / 8;  // 16-byte chunks per row segment (4 or 2)
+  // Pack and store in 16-column halves: each lane writes its row's 32-byte
+  // half-segment to the warp's buffer (two 16-byte chunks, XOR-swizzled by
+  // row pair), then each store instruction writes the half-segments of 16 rows.
 #pragma unroll
-  for (int q = 0; q < CH; ++q) {
-    uint32_t w4[4];
+  for (int hlf = 0; hlf < W / 16; ++hlf) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if constexpr (std::is_same_v<T, __nv_bfloat16>) {
-        const __nv_bfloat162 b = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
-        w4[j] = *reinterpret_cast<const uint32_t*>(&b);
-      } else {
-        const __half2 b = __floats2half2_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
-        w4[j] = *reinterpret_cast<const uint32_t*>(&b);
+    for (int q = 0; q < 2; ++q) {
+      uint32_t w4[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = v[hlf * 16 + q * 8 + 2 * j], b = v[hlf * 16 + q * 8 + 2 * j + 1];
+        if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+          const __nv_bfloat162 bb = __floats2bfloat162_rn(a, b);
+          w4[j] = *reinterpret_cast<const uint32_t*>(&bb);
+        } else {
+          const __half2 bb = __floats2half2_rn(a, b);
+          w4[j] = *reinterpret_cast<const uint32_t*>(&bb);
+        }
       }
+      *reinterpret_cast<uint4*>(wbuf + lane * 32 + ((q ^ ((lane >> 2) & 1)) * 16)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
     }
-    *reinterpret_cast<uint4*>(wbuf + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-  }
-  __syncwarp();
-  constexpr int RPI = 32 / CH;  // rows per store instruction
+    __syncwarp();
 #pragma unroll
-  for (int i = 0; i < 32 / RPI; ++i) {
-    const int lr = i * RPI + lane / CH;  // row within the warp
-    const int ch = lane % CH;
-    const int orow = __shfl_sync(0xffffffffu, r, lr);
-    const uint4 val = *reinterpret_cast<const uint4*>(wbuf + lr * 64 + ((ch ^ ((lr >> 1) & 3)) * 16));
-    if (orow >= 0) *reinterpret_cast<uint4*>(out + static_cast<int64_t>(orow) * co + col0 + c0 + ch * 8) = val;
+    for (int i = 0; i < 2; ++i) {
+      const int lr = i * 16 + lane / 2;  // row within the warp
+      const int ch = lane & 1;
+      const int orow = __shfl_sync(0xffffffffu, r, lr);
+      const uint4 val = *reinterpret_cast<const uint4*>(wbuf + lr * 32 + ((ch ^ ((lr >> 2) & 1)) * 16));
+      if (orow >= 0)
+        *reinterpret_cast<uint4*>(out + static_cast<int64_t>(orow) * co + col0 + c0 + hlf * 16 + ch * 8) = val;
+    }
+    __syncwarp();
   }
-  __syncwarp();
 }
 
 template <int KC, int BNMAX, int TPI, bool BF16>
@@ -214,7 +220,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   int32_t* idx_s = reinterpret_cast<int32_t*>(smem + S::kStages * S::kStageBytes);  // [27][TPI*128]
-  uint8_t* out_s = smem + S::kStages * S::kStageBytes + S::kIdxBytes;  // [4 warps][32 rows][32 cols]
+  uint8_t* out_s = smem + S::kStages * S::kStageBytes + S::kIdxBytes;  // [4 warps][32 rows][16 cols]
   uint64_t* bars = reinterpret_cast<uint64_t*>(out_s + S::kOutBytes);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 30);
   const uint32_t smem_base = smem_u32(smem);
@@ -427,7 +433,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const T* bias = static_cast<const T*>(p.bias);
     const T* res = static_cast<const T*>(p.residual);
     T* out = static_cast<T*>(p.out);
-    uint8_t* wbuf = out_s + (warp - (kMmaWarp + 1)) * (32 * 64);
+    uint8_t* wbuf = out_s + (warp - (kMmaWarp + 1)) * (32 * 32);
     uint32_t it = 0;
     for (int64_t item = blockIdx.x; item < p.num_items; item += gridDim.x, ++it) {
       const int64_t g = item / p.co_blocks;

@@ -49,7 +49,8 @@ cudaError_t dev_alloc(Handle* h, void** p, size_t bytes);
 void dev_free(Handle* h, void* p);
 
 // kmap construction (sc_kmap.cu)
-sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int dilation, uint32_t flags, KMap** out);
+sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t n_out, int dilation, uint32_t flags,
+                     KMap** out);
 sc_status build_down2(Handle* h, const int32_t* coords, int64_t n, uint32_t flags, KMap** out);
 sc_status build_up2(Handle* h, const KMap* down, uint32_t flags, KMap** out);
 sc_status export_map(Handle* h, const KMap* km, int32_t* map_out);

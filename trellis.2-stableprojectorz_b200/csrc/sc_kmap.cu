@@ -278,7 +278,8 @@ __device__ __forceinline__ int sorted_find(const unsigned long long* __restrict_
 
 __global__ void __launch_bounds__(128) k_probe_sorted(const int4* __restrict__ coords, int64_t n,
                                                       const unsigned long long* __restrict__ skeys,
-                                                      const uint32_t* __restrict__ svals, Packing pk, int dil,
+                                                      const uint32_t* __restrict__ svals, int64_t n_keys,
+                                                      Packing pk, int dil,
                                                       int32_t* __restrict__ map, uint32_t* __restrict__ row_mask,
                                                       unsigned long long* counters) {
   __shared__ int32_t s_map[128 * 27];
@@ -297,7 +298,7 @@ __global__ void __launch_bounds__(128) k_probe_sorted(const int4* __restrict__ c
       if (v == 13) {
         r = static_cast<int>(i);
       } else if (cok && x >= 0 && y >= 0 && z >= 0 && x <= pk.mx && y <= pk.my && z <= pk.mz) {
-        r = sorted_find(skeys, svals, n, pack_compact(c.x, x, y, z, pk));
+        r = sorted_find(skeys, svals, n_keys, pack_compact(c.x, x, y, z, pk));
       }
       s_map[threadIdx.x * 27 + v] = r;
       m |= (r >= 0 ? 1u : 0u) << v;
@@ -560,20 +561,22 @@ sc_status read_maxima(Handle* h, const int32_t* coords, int64_t n, int shift, in
 
 }  // namespace
 
-sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int dilation, uint32_t flags, KMap** out) {
+sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t n_out, int dilation, uint32_t flags,
+                     KMap** out) {
+  // Neighbours are looked up among all n input rows; outputs are rows [0, n_out).
   KMap* km = nullptr;
-  sc_status st = new_kmap(h, SC_KMAP_SUBM, 27, n, n, &km);
+  sc_status st = new_kmap(h, SC_KMAP_SUBM, 27, n, n_out, &km);
   if (st != SC_OK) return st;
   Temps tmp(h);
   st = alloc_kmap(h, km);
-  if (st != SC_OK || n == 0) {
+  if (st != SC_OK || n == 0 || n_out == 0) {
     if (st != SC_OK) free_kmap(h, km); else *out = km;
     return st;
   }
   int32_t* map;
   uint32_t* row_mask;
-  cudaError_t e = tmp.get(&map, sizeof(int32_t) * n * 27);
-  if (e == cudaSuccess) e = tmp.get(&row_mask, sizeof(uint32_t) * n);
+  cudaError_t e = tmp.get(&map, sizeof(int32_t) * n_out * 27);
+  if (e == cudaSuccess) e = tmp.get(&row_mask, sizeof(uint32_t) * n_out);
   if (e != cudaSuccess) {
     free_kmap(h, km);
     return cuda_error(h, e, "alloc map");
@@ -616,7 +619,7 @@ sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int dilation, 
     ++h->launches;
     k_check_sorted_unique<<<blocks_for(n, 256), 256, 0, h->stream>>>(sk, n, km->err);
     ++h->launches;
-    k_probe_sorted<<<blocks_for(n, 128), 128, 0, h->stream>>>(c4, n, sk, sv, pk, dilation, map, row_mask,
+    k_probe_sorted<<<blocks_for(n_out, 128), 128, 0, h->stream>>>(c4, n_out, sk, sv, n, pk, dilation, map, row_mask,
                                                                km->counters);
   } else {
     uint32_t cap = 4096;
@@ -631,7 +634,7 @@ sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int dilation, 
     ++h->launches;
     k_hash_insert<<<blocks_for(n, 256), 256, 0, h->stream>>>(c4, n, slots, cap - 1, km->err);
     ++h->launches;
-    k_probe_hash<<<blocks_for(n, 128), 128, 0, h->stream>>>(c4, n, slots, cap - 1, dilation, map, row_mask,
+    k_probe_hash<<<blocks_for(n_out, 128), 128, 0, h->stream>>>(c4, n_out, slots, cap - 1, dilation, map, row_mask,
                                                              km->counters);
   }
   e = cudaGetLastError();

@@ -160,16 +160,26 @@ def _flags(tile_sort, check):
     return f if check else f | L.SC_BUILD_DEFER_CHECK
 
 
-def build_kmap(coords, dilation=1, engine=None, tile_sort=True, check=True):
-    """Submanifold 3x3x3 neighbour map (``sc_kmap_build``)."""
+def build_kmap(coords, dilation=1, engine=None, tile_sort=True, check=True, n_out=None):
+    """Submanifold 3x3x3 neighbour map (``sc_kmap_build``).
+
+    With ``n_out`` only the first ``n_out`` rows are outputs while neighbours
+    are looked up among all rows (``sc_kmap_build_ex``; sharded convs put a
+    rank's owned voxels first and its halo after them).
+    """
     coords = _coords_arg(coords)
     eng = engine or get_engine(coords.device)
     eng.bind_stream()
     p = ctypes.c_void_p()
-    eng.check(eng.lib.sc_kmap_build(eng.handle, _ptr(coords), coords.shape[0], 3, int(dilation),
-                                    _flags(tile_sort, check), ctypes.byref(p)), "sc_kmap_build")
     n = coords.shape[0]
-    return KernelMap(eng, p, L.SC_KMAP_SUBM, n, n, 27)
+    if n_out is None:
+        eng.check(eng.lib.sc_kmap_build(eng.handle, _ptr(coords), n, 3, int(dilation),
+                                        _flags(tile_sort, check), ctypes.byref(p)), "sc_kmap_build")
+        n_out = n
+    else:
+        eng.check(eng.lib.sc_kmap_build_ex(eng.handle, _ptr(coords), n, int(n_out), 3, int(dilation),
+                                           _flags(tile_sort, check), ctypes.byref(p)), "sc_kmap_build_ex")
+    return KernelMap(eng, p, L.SC_KMAP_SUBM, n, n_out, 27)
 
 
 def build_down2(coords, engine=None, tile_sort=True):
