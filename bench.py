@@ -7,8 +7,8 @@ Ci = Co = 128, f32 accumulation.  One step = kernel-map build (hash probe,
 neighbour-mask tile sort) + the fused tcgen05 conv, on inputs resident in HBM;
 L2 is flushed (256 MB write) between steps outside the timed events.
 
-Metric: active voxels per second (whole job; every rank runs its own seeded
-shape, data-parallel, so scaling is weak).  Extra keys report the conv
+Metric: active voxels per second (whole job; every rank runs its own replica
+of the workload, data-parallel, so scaling is weak).  Extra keys report the conv
 kernel's useful TFLOP/s (2*Ci*Co*M, M = valid (output, offset) pairs) against
 the measured bf16 peak, the map-build time, the end-to-end number through the
 public Python API with host buffers, a CPU baseline, and sampled clocks.
@@ -47,7 +47,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-steps", type=int, default=3, help="timed CPU-baseline steps (rank 0, N=1)")
-    ap.add_argument("--workload", choices=["c2", "c5"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "c5", "table"], default="c2",
                     help="c2: BASELINE configs[1] (default, data-parallel across ranks); "
                          "c5: configs[4] 1024^3 Morton-sharded across ranks with NCCL halo exchange (strong scaling)")
     return ap.parse_args()
@@ -95,6 +95,16 @@ class ClockSampler:
                  "-i", str(self.dev), "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        # the timed region starts only once the sampler is producing rows
+        t_end = time.time() + 10.0
+        while time.time() < t_end and self.proc.poll() is None:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.01)
         return self
 
     def __exit__(self, *exc):
@@ -126,10 +136,11 @@ class ClockSampler:
 
 
 def make_inputs(rank):
+    """configs[1] on every rank: N data-parallel replicas of the same seeded shape."""
     import numpy as np
     import __graft_entry__
     pkg = __graft_entry__.load_package()
-    w = pkg.workloads.make_workload(2, seed=2 + 100 * rank)
+    w = pkg.workloads.make_workload(2)
     return w, np.ascontiguousarray(w.coords)
 
 
@@ -307,12 +318,12 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": 1e3 * t_total / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic: seeded union of 6 ellipsoid shells at 256^3 (BASELINE configs[1]); each rank its own seed",
+        "data": "synthetic: seeded union of 6 ellipsoid shells at 256^3 (BASELINE configs[1]); the same shape on every rank",
         "config": {"workload": w.name, "voxels_per_rank": w.n, "ci": w.ci, "co": w.co, "kernel": "3x3x3 submanifold",
                    "pairs": info["num_pairs"], "tile_pairs": info["tile_pairs"],
                    "step": "kernel-map build (hash probe + mask-sorted tiles) + fused tcgen05 conv",
                    "l2": "flushed between steps by a 256 MB write outside the timed events",
-                   "parallelism": f"data-parallel x{world} (independent shapes per rank)"},
+                   "parallelism": f"data-parallel x{world} (one replica of the workload per rank)"},
         "map_build_ms": 1e3 * t_map / args.steps, "conv_ms": 1e3 * conv_s,
         "conv_tflops": achieved, "conv_pct_of_bf16_peak": 100.0 * achieved / peak,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -446,12 +457,132 @@ def run_c5(args):
     return 0
 
 
+def _cpu_chain(idx, w, sample_rows):
+    """One CPU step of config `idx` (torch CPU restatement) on the first `sample_rows`
+    Morton-ordered voxels; returns (seconds, pairs-in-sample)."""
+    import numpy as np
+    import torch
+    from oracle import sparse_conv_ref as R
+    n = min(w.n, sample_rows)
+    c_np = np.ascontiguousarray(w.coords[:n])
+    coords = torch.from_numpy(c_np)
+    f = torch.from_numpy(w.feats[:n]).float()
+    wt = lambda a: torch.from_numpy(np.asarray(a)).to(torch.bfloat16).float()
+    t0 = time.perf_counter()
+    if idx == 4:
+        parents, dmap = R.down2_map(c_np)
+        h = R.torch_cpu_conv(f, torch.from_numpy(dmap), wt(w.weight))
+        km = R.torch_cpu_kmap(torch.from_numpy(parents), tuple(s // 2 for s in w.spatial_shape))
+        h = R.torch_cpu_conv(h, km, wt(w.extra["w_sub"]))
+        umap = R.up2_map(c_np, parents)
+        R.torch_cpu_conv(h, torch.from_numpy(umap), wt(w.extra["w_up"]))
+        pairs = int((dmap >= 0).sum() + (km >= 0).sum() + (umap >= 0).sum())
+    else:
+        km = R.torch_cpu_kmap(coords, w.spatial_shape)
+        W = torch.from_numpy(w.weight) if idx == 1 else wt(w.weight)
+        h = R.torch_cpu_conv(f, km, W)
+        if idx == 3:
+            h = torch.nn.functional.layer_norm(h, (h.shape[1],), eps=1e-6)
+            h = torch.nn.functional.silu(h)
+            h = R.torch_cpu_conv(h, km, wt(w.extra["weight2"])) + f
+        pairs = int((km >= 0).sum())
+    return time.perf_counter() - t0, pairs, n
+
+
+def run_table(args):
+    """Every BASELINE config on one GPU: map build and conv chain (median of CUDA-event
+    times, L2 flushed before each step), next to the CPU restatement on a bounded
+    Morton-prefix sample.  One JSON line per config; not the driver's headline line."""
+    import numpy as np
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    torch.set_num_threads(os.cpu_count() or 1)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, peak_src = measured_peaks()
+    eng = pkg.get_engine(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    steps = max(args.steps, 5)
+    for idx in (1, 2, 3, 4, 5):
+        w = pkg.workloads.make_workload(idx)
+        dt = torch.float32 if w.dtype == "f32" else torch.bfloat16
+        coords = torch.from_numpy(w.coords).to(dev)
+        feats = torch.from_numpy(w.feats).to(dev, dt)
+        dW = lambda a: torch.from_numpy(np.asarray(a)).to(dev, dt)
+        W1 = dW(w.weight)
+
+        def build():
+            if idx == 4:
+                d = pkg.build_down2(coords, engine=eng)
+                s = pkg.build_kmap(d.out_coords(), engine=eng, check=False)
+                return (d, s, pkg.build_up2(d))
+            return (pkg.build_kmap(coords, engine=eng, check=False),)
+
+        if idx == 3:
+            W2 = dW(w.extra["weight2"])
+            conv = lambda m: pkg.conv3d(m[0], pkg.conv3d(m[0], feats, W1, silu=True, layernorm=True), W2,
+                                        residual=feats)
+        elif idx == 4:
+            Ws, Wu = dW(w.extra["w_sub"]), dW(w.extra["w_up"])
+            conv = lambda m: pkg.conv3d(m[2], pkg.conv3d(m[1], pkg.conv3d(m[0], feats, W1), Ws), Wu)
+        else:
+            conv = lambda m: pkg.conv3d(m[0], feats, W1)
+        t_map, t_conv = [], []
+        for k in range(3 + steps):
+            flush.zero_()
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            e[0].record()
+            maps = build()
+            e[1].record()
+            conv(maps)
+            e[2].record()
+            torch.cuda.synchronize()
+            if k >= 3:
+                t_map.append(e[0].elapsed_time(e[1]))
+                t_conv.append(e[1].elapsed_time(e[2]))
+            if k < 2 + steps:
+                del maps
+        eng.synchronize()
+        infos = [m.info() for m in maps]
+        chans = {1: [(64, 64)], 2: [(128, 128)], 3: [(256, 256), (256, 256)], 5: [(32, 32)],
+                 4: [(64, 128), (128, 128), (128, 64)]}[idx]
+        if idx == 3:
+            infos = infos * 2
+        flops = sum(2.0 * ci * co * inf["num_pairs"] for (ci, co), inf in zip(chans, infos))
+        gm, gc = statistics.median(t_map), statistics.median(t_conv)
+        del maps
+        cpu_s, cpu_pairs, cpu_n = _cpu_chain(idx, w, 400_000)
+        cpu_full_ms = 1e3 * cpu_s * (w.n / cpu_n)
+        line = {
+            "table": w.name, "voxels": w.n, "pairs": [inf["num_pairs"] for inf in infos],
+            "dtype": w.dtype, "gpu_map_ms": gm, "gpu_conv_ms": gc, "gpu_total_ms": gm + gc,
+            "conv_tflops": flops / (gc * 1e-3) / 1e12,
+            "conv_pct_of_bf16_peak": 100.0 * flops / (gc * 1e-3) / 1e12 / float(peaks["bf16_tflops"]),
+            "peak_source": f"{peak_src} bf16_tflops (burst)",
+            "gpu_voxels_per_s": w.n / ((gm + gc) * 1e-3),
+            "cpu_ms": cpu_full_ms, "cpu_threads": torch.get_num_threads(),
+            "cpu_sample": ("full workload" if cpu_n == w.n else
+                           f"first {cpu_n} Morton-ordered voxels, time scaled by {w.n / cpu_n:.2f}"),
+            "speedup_vs_cpu": cpu_full_ms / (gm + gc), "steps": steps,
+            "chain": {1: "map + conv (f32 SIMT path)", 2: "map + conv", 3: "map + conv(LN,SiLU) + conv(+skip)",
+                      4: "down map + subm map + up map; down 64->128, subm 128, up 128->64",
+                      5: "map + conv"}[idx],
+        }
+        print(json.dumps(line), flush=True)
+        del coords, feats
+        torch.cuda.empty_cache()
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "c5":
         return run_c5(args)
+    if args.workload == "table":
+        return run_table(args)
     return run_ours(args)
 
 

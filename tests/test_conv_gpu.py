@@ -182,3 +182,26 @@ def test_bad_arguments_raise(pkg, cuda):
         pkg.conv3d(km, f, W)  # Ci not a multiple of 16 on the tensor-core path
     with pytest.raises(ValueError):
         pkg.conv3d(km, f[:-1], W)
+
+
+def test_large_map_tile_order_matches_unsorted_tiles(pkg, oracle, cuda):
+    # 2.2M outputs: every output row sums its offsets in the same order whatever
+    # tile it lands in, so the mask-sorted map gives a bit-identical result to
+    # the unsorted-tile map; a sample of rows is checked against the oracle.
+    w = pkg.workloads.make_workload(5, scale=0.6)
+    assert w.n > (1 << 20)
+    c = torch.from_numpy(w.coords).to(cuda)
+    km = pkg.build_kmap(c)
+    km_plain = pkg.build_kmap(c, tile_sort=False)
+    assert km.info()["num_pairs"] == km_plain.info()["num_pairs"]
+    f = torch.from_numpy(w.feats).to(cuda, torch.bfloat16)
+    W = torch.from_numpy(w.weight).to(cuda, torch.bfloat16)
+    out = pkg.conv3d(km, f, W)
+    ref = pkg.conv3d(km_plain, f, W)
+    assert torch.equal(out, ref)
+    sample = np.random.default_rng(0).choice(w.n, 20000, replace=False)
+    full = oracle.kmap_sorted(w.coords, w.spatial_shape)
+    got = km.export().cpu().numpy()
+    assert np.array_equal(got[sample], full[sample])
+    part = oracle.conv_gather(f.float().cpu().numpy(), full[sample], W.float().cpu().numpy())
+    assert rel_l2(out.float().cpu().numpy()[sample], part) < TOL[torch.bfloat16]

@@ -328,11 +328,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int j = 0; mask; ++j) {
         const int v = __ffs(mask) - 1;
         mask &= mask - 1;
+        // One shared load per tile: lane l reads the index of row
+        // RW*w + l%RW + (l/RW)*RSTEP, which is row row0 + c*RSTEP of the thread
+        // at lane c*RW + l/CPR; shuffles hand every thread its CPR rows.
+        constexpr int RW = 32 / CPR;
         int rows_idx[TPI][CPR];
 #pragma unroll
-        for (int i = 0; i < TPI; ++i)
+        for (int i = 0; i < TPI; ++i) {
+          const int mine = idx_s[(j * TPI + i) * 128 + RW * warp + (lane % RW) + (lane / RW) * RSTEP];
 #pragma unroll
-          for (int c = 0; c < CPR; ++c) rows_idx[i][c] = idx_s[(j * TPI + i) * 128 + row0 + c * RSTEP];
+          for (int c = 0; c < CPR; ++c) rows_idx[i][c] = __shfl_sync(0xffffffffu, mine, c * RW + lane / CPR);
+        }
         for (int kc = 0; kc < p.nchunks; ++kc) {
           int w = 0;
           if (lane == 0 && !abort) w = mbar_wait(empty0 + 8u * stage, phase ^ 1u, p.err) ? 1 : 0;
