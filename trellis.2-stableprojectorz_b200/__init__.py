@@ -3,8 +3,9 @@
 A drop-in for the reference sparse-conv operator (``SparseConv3d`` of
 ``src/sparse/ops/conv3d.ts`` / the ``SPARSE_CONV_BACKEND`` module of
 ``trellis2/modules/sparse/conv``): kernel-map construction (hash or one-sweep
-radix sort), a tcgen05 implicit-GEMM conv with TMA row gathers, stride-2
-down/up convs, and Morton-range sharding across GPUs.  All compute is in
+radix sort), a tcgen05 implicit-GEMM conv fed by cp.async row gathers and TMA
+weight tiles, stride-2 down/up convs, Morton-range sharding across GPUs, and a
+host-to-host pipeline that overlaps the transfers of consecutive calls.  All compute is in
 ``libsparseconv_b200.so`` (C ABI in ``include/sparse_conv_b200.h``).
 """
 from . import _lib
@@ -13,6 +14,7 @@ from .sparse_conv import (
     Engine, get_engine, KernelMap, build_kmap, build_down2, build_up2, conv3d, layernorm_silu,
     SparseTensor, SparseConv3d, SparseConvDown2, SparseConvUp2, sparse_conv3d_forward, sparse_resblock,
 )
+from .host_pipeline import HostConvPipeline
 from . import workloads
 
 __version__ = "0.1.0"

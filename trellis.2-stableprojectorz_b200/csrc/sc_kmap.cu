@@ -146,12 +146,17 @@ __device__ __noinline__ int probe_chain(const ulonglong2* __restrict__ sl, unsig
 // issued together (out-of-range neighbours read a harmless slot and are
 // discarded), and only a home slot holding another key takes the rehash slow
 // path (rare at load <= 1/4).  Neighbour keys are the voxel's packed key plus
-// packed offsets; the row mask is built in registers and the row is written
-// straight to the [N,27] map.
+// packed offsets; the row mask is built in registers and each warp's 32 rows
+// are written to the [N,27] map as one contiguous run.
 __global__ void __launch_bounds__(256) k_probe_hash(const int4* __restrict__ coords, int64_t n,
                                                     const Slot* __restrict__ slots, uint32_t cap_mask, int dil,
                                                     int32_t* __restrict__ map, uint32_t* __restrict__ row_mask,
                                                     unsigned long long* counters) {
+  // Each warp stages its 32 rows (27 ints each; stride 27 is bank-conflict
+  // free) and writes them as one contiguous run of the [N,27] map.
+  __shared__ int32_t s_rows[8][32 * 27];
+  const int lane = threadIdx.x & 31;
+  int32_t* srow = s_rows[threadIdx.x >> 5] + lane * 27;
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   uint32_t m = 0;
   if (i < n) {
@@ -176,7 +181,6 @@ __global__ void __launch_bounds__(256) k_probe_hash(const int4* __restrict__ coo
       lz[a] = static_cast<uint32_t>(z & 3);
     }
     const ulonglong2* sl = reinterpret_cast<const ulonglong2*>(slots);
-    int32_t* row = map + i * 27;
 #pragma unroll
     for (int g = 0; g < 2; ++g) {
       ulonglong2 sv[13];
@@ -199,13 +203,21 @@ __global__ void __launch_bounds__(256) k_probe_hash(const int4* __restrict__ coo
           if (sv[k].x == q) r = static_cast<int>(static_cast<uint32_t>(sv[k].y));
           else if (sv[k].x != kEmptyKey) r = probe_chain(sl, q, cap_mask);
         }
-        row[v] = r;
+        srow[v] = r;
         m |= (r >= 0 ? 1u : 0u) << v;
       }
     }
-    row[13] = static_cast<int>(i);
+    srow[13] = static_cast<int>(i);
     m |= 1u << 13;
     row_mask[i] = m;
+  }
+  __syncwarp();
+  const int64_t first = i - lane;
+  if (first < n) {
+    const int rows = static_cast<int>(min(static_cast<int64_t>(32), n - first));
+    const int32_t* src = s_rows[threadIdx.x >> 5];
+    int32_t* dst = map + first * 27;
+    for (int e = lane; e < rows * 27; e += 32) dst[e] = src[e];
   }
   unsigned cnt = __popc(m);
 #pragma unroll
