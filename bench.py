@@ -47,6 +47,10 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-steps", type=int, default=3, help="timed CPU-baseline steps (rank 0, N=1)")
+    ap.add_argument("--c5-reserve-sms", type=int, default=-1,
+                    help="c5 on >1 GPU: SMs left to NCCL while the interior conv runs beside the halo exchange; "
+                         "-1 (default): exchange first, then one conv over all owned outputs (faster at 2 GPUs, "
+                         "where the exchange is 0.04 ms)")
     ap.add_argument("--workload", choices=["c2", "c5", "table"], default="c2",
                     help="c2: BASELINE configs[1] (default, data-parallel across ranks); "
                          "c5: configs[4] 1024^3 Morton-sharded across ranks with NCCL halo exchange (strong scaling)")
@@ -225,13 +229,14 @@ def run_ours(args):
     info = km_check.info()
     eng.synchronize()
     del km_check
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
 
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    launches0 = eng.launch_count()
     with ClockSampler(dev.index) as clk:
+        # ranks leave the barrier together, after their samplers are running
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        launches0 = eng.launch_count()
         for k in range(args.steps):
             flush.zero_()
             ev[k][0].record()
@@ -366,6 +371,7 @@ def run_c5(args):
     weight = torch.from_numpy(w.weight).to(dev, torch.bfloat16)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
     for attempt in range(2):  # the first pass warms the stream-ordered memory pool
       t0.record()
       if world > 1:
@@ -374,82 +380,105 @@ def run_c5(args):
         own_c = coords.index_select(0, own).contiguous()
         plan = S.build_halo_plan(own_c, part, rank, world)
         loc_c = S.local_coords(plan, own_c)
-        own_f = feats.index_select(0, own).contiguous()
+        own_f = feats.index_select(0, S.owned_local(plan, own)).contiguous()
         buf = torch.empty((plan.n_own + plan.n_halo, w.ci), dtype=torch.bfloat16, device=dev)
         buf[:plan.n_own].copy_(own_f)
-        n_own, n_halo = plan.n_own, plan.n_halo
+        n_own, n_halo, n_int = plan.n_own, plan.n_halo, plan.n_interior
+        km_i = pkg.build_kmap(loc_c, n_out=n_int, engine=eng)
+        km_b = pkg.build_kmap(loc_c, out_begin=n_int, n_out=n_own - n_int, engine=eng)
+        kms = [km_i, km_b]
       else:
-        plan, loc_c, buf, n_own, n_halo = None, coords, feats, w.n, 0
-      km = pkg.build_kmap(loc_c, n_out=n_own, engine=eng)
+        plan, loc_c, buf, n_own, n_halo, n_int = None, coords, feats, w.n, 0, w.n
+        kms = [pkg.build_kmap(loc_c, engine=eng)]
       t1.record()
       torch.cuda.synchronize()
       setup_ms = t0.elapsed_time(t1)
-    info = km.info()
+    infos = [km.info() for km in kms]
     out = torch.empty((n_own, w.co), dtype=torch.bfloat16, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    reserve = args.c5_reserve_sms  # SMs left to the NCCL kernels while the interior conv runs
+    if plan is not None and reserve < 0:
+        kms = [pkg.build_kmap(loc_c, n_out=n_own, engine=eng)]
 
-    def layer():
-        if plan is not None:
-            S.exchange_halo(plan, buf[:n_own], out=buf)
-        pkg.conv3d(km, buf, weight, out=out)
+    def layer(ev=None):
+        """Halo exchange beside the interior conv, then the boundary conv."""
+        if plan is None or reserve < 0:
+            if plan is not None:
+                S.exchange_halo(plan, buf[:n_own], out=buf)
+            if ev: ev[1].record()
+            pkg.conv3d(kms[0], buf, weight, out=out)
+            return
+        _, work = S.exchange_halo(plan, buf[:n_own], out=buf, async_op=True)
+        eng.set_conv_ctas(n_sms - reserve)
+        pkg.conv3d(kms[0], buf, weight, out=out[:n_int])
+        eng.set_conv_ctas(0)
+        work.wait()
+        if ev: ev[1].record()
+        pkg.conv3d(kms[1], buf, weight, out=out[n_int:])
 
     for _ in range(max(args.warmup, 3)):
         flush.zero_()
         layer()
     torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    launches0 = eng.launch_count()
     with ClockSampler(dev.index) as clk:
+        # ranks leave the barrier together, after their samplers are running
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        launches0 = eng.launch_count()
         for k in range(args.steps):
             flush.zero_()
             ev[k][0].record()
-            if plan is not None:
-                S.exchange_halo(plan, buf[:n_own], out=buf)
-            ev[k][1].record()
-            pkg.conv3d(km, buf, weight, out=out)
+            layer(ev[k])
             ev[k][2].record()
         torch.cuda.synchronize()
     launches = eng.launch_count() - launches0
     eng.synchronize()
     t_total = sum(e[0].elapsed_time(e[2]) for e in ev) / 1e3
-    t_xchg = sum(e[0].elapsed_time(e[1]) for e in ev) / 1e3
-    t_conv = sum(e[1].elapsed_time(e[2]) for e in ev) / 1e3
+    t_first = sum(e[0].elapsed_time(e[1]) for e in ev) / 1e3  # exchange + interior conv (overlapped)
+    t_last = sum(e[1].elapsed_time(e[2]) for e in ev) / 1e3   # boundary conv
+    per_rank = [t_total]
     if dist is not None:
-        tt = torch.tensor([t_total, t_xchg, t_conv, setup_ms], device=dev, dtype=torch.float64)
+        allt = [torch.zeros(1, device=dev, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(allt, torch.tensor([t_total], device=dev, dtype=torch.float64))
+        per_rank = [float(x.item()) for x in allt]
+        tt = torch.tensor([t_total, t_first, t_last, setup_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_total, t_xchg, t_conv, setup_ms = tt.tolist()
-        hh = torch.tensor([n_halo, info["num_pairs"]], device=dev, dtype=torch.float64)
+        t_total, t_first, t_last, setup_ms = tt.tolist()
+        hh = torch.tensor([n_halo, sum(i["num_pairs"] for i in infos), n_int], device=dev, dtype=torch.float64)
         dist.all_reduce(hh)
-        halo_total, pairs = int(hh[0]), int(hh[1])
+        halo_total, pairs, int_total = int(hh[0]), int(hh[1]), int(hh[2])
         dist.barrier()
         dist.destroy_process_group()
     else:
-        halo_total, pairs = 0, info["num_pairs"]
+        halo_total, pairs, int_total = 0, infos[0]["num_pairs"], w.n
     if rank != 0:
         return 0
     value = w.n * args.steps / t_total
     flops = 2.0 * w.ci * w.co * pairs
-    achieved_gbs = (w.n * (w.ci + w.co) * 2) / (t_conv / args.steps) / 1e9  # all ranks together
+    achieved_gbs = (w.n * (w.ci + w.co) * 2) / (t_total / args.steps) / 1e9  # all ranks together
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": 1e3 * t_total / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded union of 4 ellipsoid shells + 5% interior fill at 1024^3 (BASELINE configs[4])",
         "config": {"workload": w.name, "voxels": w.n, "ci": w.ci, "co": w.co, "pairs": pairs,
-                   "halo_voxels_total": halo_total,
-                   "step": "halo exchange (NCCL all_to_all_single) + fused tcgen05 conv on owned outputs; "
-                           "plan and map built once per coord set",
+                   "halo_voxels_total": halo_total, "interior_voxels_total": int_total,
+                   "step": ("halo exchange (NCCL all_to_all_single), then the conv of all owned outputs"
+                            if reserve < 0 or world == 1 else
+                            "halo exchange (NCCL all_to_all_single) beside the conv of interior outputs "
+                            f"(on {n_sms - reserve} of {n_sms} SMs), then the conv of boundary outputs") +
+                           "; plan and maps built once per coord set",
                    "l2": "flushed between steps by a 256 MB write outside the timed events",
                    "parallelism": f"Morton-range sharding x{world}"},
-        "setup_ms": setup_ms, "exchange_ms": 1e3 * t_xchg / args.steps, "conv_ms": 1e3 * t_conv / args.steps,
-        "conv_tflops_total": flops / (t_conv / args.steps) / 1e12,
+        "setup_ms": setup_ms, "exchange_and_interior_ms": 1e3 * t_first / args.steps,
+        "boundary_ms": 1e3 * t_last / args.steps, "ms_per_step_by_rank": [1e3 * t / args.steps for t in per_rank],
+        "conv_tflops_total": flops / (t_total / args.steps) / 1e12,
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": float(peaks["hbm_gbs"]) * world,
                      "unit": "GB/s", "frac": achieved_gbs / (float(peaks["hbm_gbs"]) * world),
                      "peak_source": f"{peak_src} hbm_gbs x n_gpus",
-                     "units": "feature bytes in + out (N*(Ci+Co)*2) per conv, summed over ranks"},
+                     "units": "feature bytes in + out (N*(Ci+Co)*2) per layer step, summed over ranks"},
         "clocks": clk.summary(), "gpu_launches": launches,
     }
     print(json.dumps(line), flush=True)

@@ -103,6 +103,11 @@ SC_API sc_status sc_create(sc_handle** out, const sc_config* cfg);
 SC_API sc_status sc_destroy(sc_handle* h);
 /* Enqueue all later work on `stream` (a cudaStream_t; NULL = legacy default). */
 SC_API sc_status sc_set_stream(sc_handle* h, void* stream);
+
+/* CTAs of the persistent tensor-core conv: 0 (default) = one per SM.  A
+ * smaller grid leaves SMs free for a collective that runs beside the conv
+ * (the halo exchange of a sharded conv).  No counterpart in the reference. */
+SC_API sc_status sc_set_conv_ctas(sc_handle* h, int32_t max_ctas);
 /* Waits for all work enqueued on the handle's stream. */
 SC_API sc_status sc_synchronize(sc_handle* h);
 /* Human-readable description of the last error on this handle. */
@@ -125,6 +130,16 @@ SC_API sc_status sc_kmap_build(sc_handle* h, const int32_t* coords, int64_t n, i
  * ranks) after them.  Replaces the same passes as sc_kmap_build. */
 SC_API sc_status sc_kmap_build_ex(sc_handle* h, const int32_t* coords, int64_t n_in, int64_t n_out,
                                   int32_t kernel_size, int32_t dilation, uint32_t flags, sc_kmap** out);
+
+/* As sc_kmap_build_ex, with outputs rows [out_begin, out_end) of `coords`
+ * (map row j is output j = input row out_begin + j); neighbours are looked up
+ * among all n_in rows.  A sharded conv orders a rank's owned voxels interior
+ * first (no neighbour position owned by another rank), then boundary, then its
+ * halo, and builds one map per output range so the interior conv can run
+ * while the halo is in flight.  Replaces the same passes as sc_kmap_build. */
+SC_API sc_status sc_kmap_build_range(sc_handle* h, const int32_t* coords, int64_t n_in, int64_t out_begin,
+                                     int64_t out_end, int32_t kernel_size, int32_t dilation, uint32_t flags,
+                                     sc_kmap** out);
 
 /* Stride-2 2x2x2 down-sample map: parents are the unique (b, x>>1, y>>1, z>>1)
  * in ascending lexicographic order; map column = (x&1)*4 + (y&1)*2 + (z&1).

@@ -47,6 +47,8 @@ def _worker(rank, world, port, cfg, scale):
         own = part.owned_rows(coords, rank)
         own_coords = coords.index_select(0, own).contiguous()
         plan = S.build_halo_plan(own_coords, part, rank, world)
+        own = S.owned_local(plan, own)  # global row of each local owned row
+        assert torch.equal(torch.sort(own).values, part.owned_rows(coords, rank))
         feats = torch.from_numpy(w.feats[:, :16].copy())
         loc_f = S.exchange_halo(plan, feats.index_select(0, own))
         loc_c = S.local_coords(plan, own_coords)
@@ -62,6 +64,9 @@ def _worker(rank, world, port, cfg, scale):
         km_glob = R.kmap_sorted(w.coords, w.spatial_shape)[own.numpy()]
         translated = np.where(km_loc >= 0, gid[np.maximum(km_loc, 0)], -1)
         assert np.array_equal(translated, km_glob)
+        # interior rows (first in plan order) read no halo row; some rows are interior
+        assert (km_loc[:plan.n_interior] < plan.n_own).all()
+        assert 0 < plan.n_interior <= plan.n_own
         # owned conv outputs equal the single-rank conv
         W = torch.from_numpy(w.weight[:16, :, :, :, :16].copy())
         out = R.torch_cpu_conv(loc_f, torch.from_numpy(km_loc), W)

@@ -51,12 +51,30 @@ def _worker(rank, world, port, cfg, scale, ch):
         own = part.owned_rows(coords, rank)
         own_c = coords.index_select(0, own).contiguous()
         plan = S.build_halo_plan(own_c, part, rank, world)
+        own = S.owned_local(plan, own)  # global row of each local owned row
+        loc_c = S.local_coords(plan, own_c)
         loc_f = S.exchange_halo(plan, feats.index_select(0, own))
-        km = pkg.build_kmap(S.local_coords(plan, own_c), n_out=plan.n_own)
+        km = pkg.build_kmap(loc_c, n_out=plan.n_own)
         out = pkg.conv3d(km, loc_f, W)
         torch.cuda.synchronize()
         assert out.shape == (plan.n_own, ch)
         assert torch.equal(out, ref.index_select(0, own))
+        # interior outputs while the halo is in flight, then boundary outputs
+        ni = plan.n_interior
+        km_i = pkg.build_kmap(loc_c, n_out=ni)
+        km_b = pkg.build_kmap(loc_c, out_begin=ni, n_out=plan.n_own - ni)
+        buf = torch.zeros_like(loc_f)
+        buf[:plan.n_own].copy_(feats.index_select(0, own))
+        split = torch.empty_like(out)
+        eng = pkg.get_engine(dev)
+        eng.set_conv_ctas(torch.cuda.get_device_properties(dev).multi_processor_count - 16)
+        _, work = S.exchange_halo(plan, buf[:plan.n_own], out=buf, async_op=True)
+        pkg.conv3d(km_i, buf, W, out=split[:ni])
+        work.wait()
+        eng.set_conv_ctas(0)
+        pkg.conv3d(km_b, buf, W, out=split[ni:])
+        torch.cuda.synchronize()
+        assert torch.equal(split, out)
     finally:
         dist.destroy_process_group()
 

@@ -71,11 +71,13 @@ _SIGNATURES = {
     "sc_create": (_I32, [_PP, ctypes.POINTER(ScConfig)]),
     "sc_destroy": (_I32, [_P]),
     "sc_set_stream": (_I32, [_P, _P]),
+    "sc_set_conv_ctas": (_I32, [_P, _I32]),
     "sc_synchronize": (_I32, [_P]),
     "sc_last_error": (ctypes.c_char_p, [_P]),
     "sc_launch_count": (ctypes.c_uint64, [_P]),
     "sc_kmap_build": (_I32, [_P, _P, _I64, _I32, _I32, _U32, _PP]),
     "sc_kmap_build_ex": (_I32, [_P, _P, _I64, _I64, _I32, _I32, _U32, _PP]),
+    "sc_kmap_build_range": (_I32, [_P, _P, _I64, _I64, _I64, _I32, _I32, _U32, _PP]),
     "sc_kmap_build_down2": (_I32, [_P, _P, _I64, _U32, _PP]),
     "sc_kmap_build_up2": (_I32, [_P, _P, _U32, _PP]),
     "sc_kmap_build_noalloc": (_I32, [_P, _P, _I64, _I32, _P]),

@@ -152,6 +152,13 @@ sc_status sc_destroy(sc_handle* h) {
   return SC_OK;
 }
 
+sc_status sc_set_conv_ctas(sc_handle* h, int32_t max_ctas) {
+  if (!h) return SC_EINVAL;
+  if (max_ctas < 0) return sc::set_error(&h->impl, SC_EINVAL, "max_ctas must be >= 0");
+  h->impl.conv_ctas = max_ctas;
+  return SC_OK;
+}
+
 sc_status sc_set_stream(sc_handle* h, void* stream) {
   if (!h) return SC_EINVAL;
   h->impl.stream = static_cast<cudaStream_t>(stream);
@@ -194,27 +201,34 @@ sc_status sc_kmap_build(sc_handle* h, const int32_t* coords, int64_t n, int32_t 
   if (dilation < 1 || dilation > 1024) return sc::set_error(H, SC_EINVAL, "dilation must be in [1, 1024]");
   sc::DeviceGuard g(H->device);
   KMap* km = nullptr;
-  const sc_status st = sc::build_subm(H, coords, n, n, dilation, flags, &km);
+  const sc_status st = sc::build_subm(H, coords, n, 0, n, dilation, flags, &km);
   if (st != SC_OK) return st;
   return wrap_kmap(H, km, flags, out);
 }
 
-sc_status sc_kmap_build_ex(sc_handle* h, const int32_t* coords, int64_t n_in, int64_t n_out, int32_t kernel_size,
-                           int32_t dilation, uint32_t flags, sc_kmap** out) {
+sc_status sc_kmap_build_range(sc_handle* h, const int32_t* coords, int64_t n_in, int64_t out_begin, int64_t out_end,
+                              int32_t kernel_size, int32_t dilation, uint32_t flags, sc_kmap** out) {
   if (!h || !out) return SC_EINVAL;
   *out = nullptr;
   Handle* H = &h->impl;
   if (n_in < 0 || n_in >= (1ll << 29)) return sc::set_error(H, SC_EINVAL, "n_in must be in [0, 2^29)");
-  if (n_out < 0 || n_out > n_in) return sc::set_error(H, SC_EINVAL, "n_out must be in [0, n_in]");
+  if (out_begin < 0 || out_end < out_begin || out_end > n_in)
+    return sc::set_error(H, SC_EINVAL, "need 0 <= out_begin <= out_end <= n_in");
   if (n_in > 0 && (!coords || !sc::aligned(coords, 16)))
     return sc::set_error(H, SC_EINVAL, "coords must be a 16-byte aligned device pointer");
   if (kernel_size != 3) return sc::set_error(H, SC_EUNSUPPORTED, "only 3x3x3 submanifold kernels");
   if (dilation < 1 || dilation > 1024) return sc::set_error(H, SC_EINVAL, "dilation must be in [1, 1024]");
   sc::DeviceGuard g(H->device);
   KMap* km = nullptr;
-  const sc_status st = sc::build_subm(H, coords, n_in, n_out, dilation, flags, &km);
+  const sc_status st = sc::build_subm(H, coords, n_in, out_begin, out_end - out_begin, dilation, flags, &km);
   if (st != SC_OK) return st;
   return wrap_kmap(H, km, flags, out);
+}
+
+sc_status sc_kmap_build_ex(sc_handle* h, const int32_t* coords, int64_t n_in, int64_t n_out, int32_t kernel_size,
+                           int32_t dilation, uint32_t flags, sc_kmap** out) {
+  if (h && (n_out < 0 || n_out > n_in)) return sc::set_error(&h->impl, SC_EINVAL, "n_out must be in [0, n_in]");
+  return sc_kmap_build_range(h, coords, n_in, 0, n_out, kernel_size, dilation, flags, out);
 }
 
 sc_status sc_kmap_build_down2(sc_handle* h, const int32_t* coords, int64_t n, uint32_t flags, sc_kmap** out) {

@@ -53,6 +53,7 @@ struct TcParams {
   const void* bias;
   const void* residual;
   void* out;
+  const int32_t* group_order;  // groups by descending work (null: natural order)
   int64_t num_items;  // tile groups * co_blocks
   int64_t num_tiles;
   int co_blocks;
@@ -68,6 +69,7 @@ struct TcParams {
 
 constexpr int kProducers = 128;  // warps 0-3
 constexpr int kMmaWarp = 4;
+constexpr int64_t kWorkOrderMaxItemsPerCta = 64;
 constexpr int kTcThreads = 288;
 
 // Shared-memory plan for one CTA.  A stage holds TPI gathered A tiles
@@ -255,7 +257,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem_base = *s_tmem;
   const int bn = p.bn;
   // An item is a group of TPI consecutive tiles times one block of bn output
-  // channels; the group runs the union of its tiles' offsets.
+  // channels; the group runs the union of its tiles' offsets.  Items are taken
+  // in the map's work order (groups by descending offset count) in rounds of
+  // gridDim.x, this CTA taking position blockIdx.x of even rounds and
+  // gridDim.x-1-blockIdx.x of odd rounds, so every CTA gets about the same
+  // work (static striding of the natural order left the busiest CTA ~18%
+  // above the mean on the 256^3 workload).  All three roles walk the same
+  // sequence.
+  auto next_item = [&](int64_t& r) -> int64_t {  // item of round >= r (r updated), -1 when done
+    for (;; ++r) {
+      if (r * static_cast<int64_t>(gridDim.x) >= p.num_items) return -1;
+      const int64_t pos = (r & 1) ? static_cast<int64_t>(gridDim.x) - 1 - blockIdx.x : blockIdx.x;
+      const int64_t j = r * static_cast<int64_t>(gridDim.x) + pos;
+      if (j < p.num_items) return j;
+    }
+  };
+  auto item_group = [&](int64_t j, int& cb) -> int64_t {
+    const int64_t q = j / p.co_blocks;
+    cb = static_cast<int>(j - q * p.co_blocks);
+    return p.group_order ? static_cast<int64_t>(__ldg(p.group_order + q)) : q;
+  };
   auto group_mask = [&](int64_t g) {
     uint32_t m = 0;
 #pragma unroll
@@ -287,7 +308,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // gather-index prefetch: warp w loads active offsets j = w, w+4, ... (<= 7 each)
     int4 pre[7][TPI];
     auto load_idx = [&](int64_t item) {
-      const int64_t g = item / p.co_blocks;
+      int cb_unused;
+      const int64_t g = item_group(item, cb_unused);
       const uint32_t m = group_mask(g);
       const int nact = __popc(m);
 #pragma unroll
@@ -316,14 +338,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
     };
-    int64_t item = blockIdx.x;
-    if (item < p.num_items) store_idx(load_idx(item));
-    for (; item < p.num_items; item += gridDim.x) {
+    int64_t round = 0;
+    int64_t item = next_item(round);
+    if (item >= 0) store_idx(load_idx(item));
+    while (item >= 0) {
       named_bar_sync(1, kProducers);  // idx_s holds this group's indices
-      const int64_t g = item / p.co_blocks;
-      const int cb = static_cast<int>(item - g * p.co_blocks);
-      const int64_t next = item + gridDim.x;
-      const int nact_next = next < p.num_items ? load_idx(next) : 0;
+      int cb;
+      const int64_t g = item_group(item, cb);
+      int64_t round_next = round + 1;
+      const int64_t next = next_item(round_next);
+      const int nact_next = next >= 0 ? load_idx(next) : 0;
       uint32_t mask = group_mask(g);
       for (int j = 0; mask; ++j) {
         const int v = __ffs(mask) - 1;
@@ -373,10 +397,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       }
-      if (next < p.num_items) {
+      if (next >= 0) {
         named_bar_sync(1, kProducers);  // every producer has read this group's indices
         store_idx(nact_next);
       }
+      round = round_next;
+      item = next;
     }
     cp_async_wait_all();
     if (abort && pt == 0) {
@@ -391,8 +417,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int stage = 0;
       uint32_t phase = 0, it = 0;
       bool ok = true;
-      for (int64_t item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++it) {
-        const int64_t g = item / p.co_blocks;
+      int64_t round = 0;
+      for (int64_t item = next_item(round); ok && item >= 0; ++round, item = next_item(round), ++it) {
+        int cb_unused;
+        const int64_t g = item_group(item, cb_unused);
         const uint32_t acc = it & 1u, aph = (it >> 1) & 1u;
         if (!mbar_wait(tempty0 + 8u * acc, aph ^ 1u, p.err)) break;
         tc_fence_after();
@@ -441,9 +469,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     T* out = static_cast<T*>(p.out);
     uint8_t* wbuf = out_s + (warp - (kMmaWarp + 1)) * (32 * 32);
     uint32_t it = 0;
-    for (int64_t item = blockIdx.x; item < p.num_items; item += gridDim.x, ++it) {
-      const int64_t g = item / p.co_blocks;
-      const int cb = static_cast<int>(item - g * p.co_blocks);
+    int64_t round = 0;
+    for (int64_t item = next_item(round); item >= 0; ++round, item = next_item(round), ++it) {
+      int cb;
+      const int64_t g = item_group(item, cb);
       const uint32_t acc = it & 1u, aph = (it >> 1) & 1u;
       int w = 1;
       if (lane == 0) w = mbar_wait(tfull0 + 8u * acc, aph, p.err) ? 1 : 0;
@@ -532,7 +561,12 @@ sc_status launch_tc(Handle* h, const KMap* km, const void* feats, const void* we
   auto kern = conv_tc_kernel<KC, BNMAX, TPI, BF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
   if (e != cudaSuccess) return cuda_error(h, e, "conv smem attribute");
-  const int64_t grid = std::min<int64_t>(p.num_items, h->num_sms);
+  const int64_t ctas = h->conv_ctas > 0 ? std::min(h->conv_ctas, h->num_sms) : h->num_sms;
+  const int64_t grid = std::min<int64_t>(p.num_items, ctas);
+  // Work order balances CTAs that run few items (10 per CTA on the 256^3
+  // workload: -9% conv time); with many items per CTA static striding is
+  // already balanced and the natural tile order keeps better L2 locality.
+  p.group_order = p.num_items < kWorkOrderMaxItemsPerCta * grid ? km->group_order[TPI - 1] : nullptr;
   ++h->launches;
   kern<<<static_cast<unsigned>(grid), kTcThreads, S::kSmemBytes, h->stream>>>(tb, p);
   e = cudaGetLastError();

@@ -16,6 +16,7 @@ struct Handle {
   int debug_bounds = 0;
   cudaStream_t stream = nullptr;
   int num_sms = 148;
+  int conv_ctas = 0;  // CTAs of the tensor-core conv; 0 = one per SM
   int* derr = nullptr;  // device error word written by conv kernels
   unsigned long long launches = 0;  // kernels this handle has launched
   std::string last_error;
@@ -38,6 +39,9 @@ struct KMap {
   int32_t* gidx = nullptr;
   int32_t* tile_rows = nullptr;
   uint32_t* tile_mask = nullptr;
+  // Groups of TPI = 1, 2 consecutive tiles ordered by descending work (number
+  // of offsets the group runs); the conv schedules its items in this order.
+  int32_t* group_order[2] = {nullptr, nullptr};
   int32_t* out_coords = nullptr;   // down-sample: parent coords [n_out, 4]
   int32_t* parent_of = nullptr;    // down-sample: parent of every fine row [n_in]
   unsigned long long* counters = nullptr;  // [0] valid pairs, [1] tile pairs
@@ -49,8 +53,8 @@ cudaError_t dev_alloc(Handle* h, void** p, size_t bytes);
 void dev_free(Handle* h, void* p);
 
 // kmap construction (sc_kmap.cu)
-sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t n_out, int dilation, uint32_t flags,
-                     KMap** out);
+sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t out_begin, int64_t n_out, int dilation,
+                     uint32_t flags, KMap** out);
 sc_status build_down2(Handle* h, const int32_t* coords, int64_t n, uint32_t flags, KMap** out);
 sc_status build_up2(Handle* h, const KMap* down, uint32_t flags, KMap** out);
 sc_status export_map(Handle* h, const KMap* km, int32_t* map_out);

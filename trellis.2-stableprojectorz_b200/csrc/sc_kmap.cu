@@ -148,7 +148,7 @@ __device__ __noinline__ int probe_chain(const ulonglong2* __restrict__ sl, unsig
 // path (rare at load <= 1/4).  Neighbour keys are the voxel's packed key plus
 // packed offsets; the row mask is built in registers and each warp's 32 rows
 // are written to the [N,27] map as one contiguous run.
-__global__ void __launch_bounds__(256) k_probe_hash(const int4* __restrict__ coords, int64_t n,
+__global__ void __launch_bounds__(256) k_probe_hash(const int4* __restrict__ coords, int64_t n, int64_t row_base,
                                                     const Slot* __restrict__ slots, uint32_t cap_mask, int dil,
                                                     int32_t* __restrict__ map, uint32_t* __restrict__ row_mask,
                                                     unsigned long long* counters) {
@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(256) k_probe_hash(const int4* __restrict__ coo
         m |= (r >= 0 ? 1u : 0u) << v;
       }
     }
-    srow[13] = static_cast<int>(i);
+    srow[13] = static_cast<int>(row_base + i);
     m |= 1u << 13;
     row_mask[i] = m;
   }
@@ -289,7 +289,7 @@ __device__ __forceinline__ int sorted_find(const unsigned long long* __restrict_
   return (lo < n && __ldg(skeys + lo) == q) ? static_cast<int>(__ldg(svals + lo)) : -1;
 }
 
-__global__ void __launch_bounds__(128) k_probe_sorted(const int4* __restrict__ coords, int64_t n,
+__global__ void __launch_bounds__(128) k_probe_sorted(const int4* __restrict__ coords, int64_t n, int64_t row_base,
                                                       const unsigned long long* __restrict__ skeys,
                                                       const uint32_t* __restrict__ svals, int64_t n_keys,
                                                       Packing pk, int dil,
@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(128) k_probe_sorted(const int4* __restrict__ c
       const int x = c.y + dx, y = c.z + dy, z = c.w + dz;
       int r = -1;
       if (v == 13) {
-        r = static_cast<int>(i);
+        r = static_cast<int>(row_base + i);
       } else if (cok && x >= 0 && y >= 0 && z >= 0 && x <= pk.mx && y <= pk.my && z <= pk.mz) {
         r = sorted_find(skeys, svals, n_keys, pack_compact(c.x, x, y, z, pk));
       }
@@ -504,6 +504,10 @@ sc_status alloc_kmap(Handle* h, KMap* km) {
   SC_TRY_CUDA(dev_alloc(h, reinterpret_cast<void**>(&km->tile_mask),
                         sizeof(uint32_t) * std::max<int64_t>(km->num_tiles, 1)),
               "alloc tile_mask");
+  for (int t = 0; t < 2; ++t)
+    SC_TRY_CUDA(dev_alloc(h, reinterpret_cast<void**>(&km->group_order[t]),
+                          sizeof(int32_t) * std::max<int64_t>((km->num_tiles + t) / (t + 1), 1)),
+                "alloc group order");
   return SC_OK;
 }
 
@@ -537,6 +541,51 @@ __global__ void k_sort_keys(const uint32_t* __restrict__ row_mask, int64_t n, in
   keys[i] = k;
 }
 
+// Work order of tile groups for the conv's scheduler: groups of `tpi`
+// consecutive tiles bucketed by the number of offsets they run (descending),
+// a counting sort in two passes (bucket sizes, then placement).  The order
+// within a bucket depends on atomic timing; conv results do not, since every
+// output row sums its offsets in the same order whichever CTA computes it.
+constexpr int kWorkBuckets = 33;  // offsets per group: 0..32
+
+__device__ __forceinline__ int group_bucket(const uint32_t* tile_mask, int64_t g, int64_t num_tiles, int tpi) {
+  uint32_t m = 0;
+  for (int i = 0; i < tpi; ++i)
+    if (g * tpi + i < num_tiles) m |= tile_mask[g * tpi + i];
+  return 32 - __popc(m);  // more offsets first
+}
+
+__global__ void k_group_hist(const uint32_t* __restrict__ tile_mask, int64_t num_tiles, int tpi, int64_t groups,
+                             uint32_t* hist) {
+  __shared__ uint32_t sh[kWorkBuckets];
+  for (int b = threadIdx.x; b < kWorkBuckets; b += blockDim.x) sh[b] = 0;
+  __syncthreads();
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    atomicAdd(&sh[group_bucket(tile_mask, g, num_tiles, tpi)], 1u);
+  __syncthreads();
+  for (int b = threadIdx.x; b < kWorkBuckets; b += blockDim.x)
+    if (sh[b]) atomicAdd(&hist[b], sh[b]);
+}
+
+__global__ void k_group_place(const uint32_t* __restrict__ tile_mask, int64_t num_tiles, int tpi, int64_t groups,
+                              const uint32_t* __restrict__ hist, uint32_t* cursor, int32_t* order) {
+  __shared__ uint32_t base[kWorkBuckets];
+  if (threadIdx.x == 0) {
+    uint32_t acc = 0;
+    for (int b = 0; b < kWorkBuckets; ++b) {
+      base[b] = acc;
+      acc += hist[b];
+    }
+  }
+  __syncthreads();
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int b = group_bucket(tile_mask, g, num_tiles, tpi);
+    order[base[b] + atomicAdd(&cursor[b], 1u)] = static_cast<int32_t>(g);
+  }
+}
+
 // Orders output rows by neighbour mask and writes gidx / tile_rows / tile_mask.
 sc_status finish_tiles(Handle* h, KMap* km, const int32_t* map, uint32_t* row_mask, uint32_t flags, Temps& tmp) {
   const int64_t n = km->n_out;
@@ -566,6 +615,20 @@ sc_status finish_tiles(Handle* h, KMap* km, const int32_t* map, uint32_t* row_ma
   ++h->launches;
   k_build_tiles<<<static_cast<unsigned>(km->num_tiles), kTileRows, 0, h->stream>>>(
       map, km->K, order, n, row_mask, km->gidx, km->tile_rows, km->tile_mask, km->counters);
+  uint32_t* counts;
+  SC_TRY_CUDA(tmp.get(&counts, sizeof(uint32_t) * 4 * kWorkBuckets), "alloc group counts");
+  SC_TRY_CUDA(cudaMemsetAsync(counts, 0, sizeof(uint32_t) * 4 * kWorkBuckets, h->stream), "clear group counts");
+  for (int t = 0; t < 2; ++t) {
+    const int tpi = t + 1;
+    const int64_t groups = (km->num_tiles + t) / tpi;
+    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((groups + 255) / 256, 4 * h->num_sms));
+    uint32_t* hist = counts + 2 * t * kWorkBuckets;
+    ++h->launches;
+    k_group_hist<<<blocks, 256, 0, h->stream>>>(km->tile_mask, km->num_tiles, tpi, groups, hist);
+    ++h->launches;
+    k_group_place<<<blocks, 256, 0, h->stream>>>(km->tile_mask, km->num_tiles, tpi, groups, hist,
+                                                 hist + kWorkBuckets, km->group_order[t]);
+  }
   SC_TRY_CUDA(cudaGetLastError(), "tile build launch");
   return SC_OK;
 }
@@ -605,9 +668,10 @@ sc_status read_maxima(Handle* h, const int32_t* coords, int64_t n, int shift, in
 
 }  // namespace
 
-sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t n_out, int dilation, uint32_t flags,
-                     KMap** out) {
-  // Neighbours are looked up among all n input rows; outputs are rows [0, n_out).
+sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t out_begin, int64_t n_out, int dilation,
+                     uint32_t flags, KMap** out) {
+  // Neighbours are looked up among all n input rows; output j is input row
+  // out_begin + j, for j in [0, n_out).
   KMap* km = nullptr;
   sc_status st = new_kmap(h, SC_KMAP_SUBM, 27, n, n_out, &km);
   if (st != SC_OK) return st;
@@ -663,8 +727,8 @@ sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t n_out,
     ++h->launches;
     k_check_sorted_unique<<<blocks_for(n, 256), 256, 0, h->stream>>>(sk, n, km->err);
     ++h->launches;
-    k_probe_sorted<<<blocks_for(n_out, 128), 128, 0, h->stream>>>(c4, n_out, sk, sv, n, pk, dilation, map, row_mask,
-                                                               km->counters);
+    k_probe_sorted<<<blocks_for(n_out, 128), 128, 0, h->stream>>>(c4 + out_begin, n_out, out_begin, sk, sv, n, pk,
+                                                               dilation, map, row_mask, km->counters);
   } else {
     uint32_t cap = 4096;
     while (cap < 4 * n) cap <<= 1;
@@ -678,8 +742,8 @@ sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t n_out,
     ++h->launches;
     k_hash_insert<<<blocks_for(n, 256), 256, 0, h->stream>>>(c4, n, slots, cap - 1, km->err);
     ++h->launches;
-    k_probe_hash<<<blocks_for(n_out, 256), 256, 0, h->stream>>>(c4, n_out, slots, cap - 1, dilation, map, row_mask,
-                                                             km->counters);
+    k_probe_hash<<<blocks_for(n_out, 256), 256, 0, h->stream>>>(c4 + out_begin, n_out, out_begin, slots, cap - 1,
+                                                             dilation, map, row_mask, km->counters);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -848,6 +912,8 @@ void free_kmap(Handle* h, KMap* km) {
   dev_free(h, km->gidx);
   dev_free(h, km->tile_rows);
   dev_free(h, km->tile_mask);
+  dev_free(h, km->group_order[0]);
+  dev_free(h, km->group_order[1]);
   dev_free(h, km->out_coords);
   dev_free(h, km->parent_of);
   dev_free(h, km->counters);

@@ -14,9 +14,13 @@ each conv every rank receives the features of those neighbours (its halo).
   voxels s never reads).
 * The plan (send lists, split sizes, halo coords) is built once per coord set
   and reused by every conv layer on those coords, like the neighbour map.
+* The plan orders a rank's owned rows interior first: rows none of whose 26
+  neighbour positions lies in another rank's range read no halo row, so their
+  outputs can be computed while the halo is in flight; boundary rows follow.
 * Per layer the exchange is one ``all_to_all_single`` (NCCL on GPUs, gloo on
   CPU ranks) of the packed send rows into the halo rows of the local feature
-  buffer: owned rows first, then halo rows grouped by source rank.
+  buffer: owned rows first (in plan order), then halo rows grouped by source
+  rank.
 
 The plan logic is device-agnostic torch code, so the same functions run on CPU
 ranks (gloo) in the tests and on GPUs (NCCL) in the benchmark.
@@ -27,7 +31,8 @@ import dataclasses
 
 import torch
 
-__all__ = ["morton_codes", "MortonPartition", "HaloPlan", "build_halo_plan", "exchange_halo", "local_coords"]
+__all__ = ["morton_codes", "MortonPartition", "HaloPlan", "build_halo_plan", "exchange_halo", "local_coords",
+           "owned_local"]
 
 _OFFS26 = [(dx, dy, dz) for dx in (-1, 0, 1) for dy in (-1, 0, 1) for dz in (-1, 0, 1) if (dx, dy, dz) != (0, 0, 0)]
 
@@ -79,7 +84,9 @@ class HaloPlan:
     rank: int
     world: int
     n_own: int
-    send_idx: torch.Tensor      # owned rows to pack, grouped by destination rank
+    n_interior: int             # local rows [0, n_interior) read no halo row
+    order: torch.Tensor         # local owned row k is the caller's owned row order[k]
+    send_idx: torch.Tensor      # local owned rows to pack, grouped by destination rank
     send_splits: list           # rows sent to each rank
     recv_splits: list           # rows received from each rank
     halo_coords: torch.Tensor   # (n_halo, 4) int32, grouped by source rank
@@ -103,9 +110,14 @@ def build_halo_plan(owned_coords, partition, rank, world, group=None):
         own = torch.where(ok, own, torch.full_like(own, rank))
         need[own, torch.arange(n, device=dev)] = True
     need[rank] = False
+    boundary = need.any(0)
+    order = torch.cat([torch.nonzero(~boundary).squeeze(1), torch.nonzero(boundary).squeeze(1)])
+    n_interior = int(n - int(boundary.sum()))
+    local_of = torch.empty_like(order)
+    local_of[order] = torch.arange(n, device=dev)
     idx, splits = [], []
     for s in range(world):
-        rows = torch.nonzero(need[s]).squeeze(1)
+        rows = local_of[torch.nonzero(need[s]).squeeze(1)]
         idx.append(rows)
         splits.append(int(rows.numel()))
     send_idx = torch.cat(idx) if idx else torch.zeros(0, dtype=torch.int64, device=dev)
@@ -114,21 +126,30 @@ def build_halo_plan(owned_coords, partition, rank, world, group=None):
     dist.all_to_all_single(rc, sc, group=group)
     recv_splits = [int(v) for v in rc.tolist()]
     halo = torch.empty((sum(recv_splits), 4), dtype=owned_coords.dtype, device=dev)
-    dist.all_to_all_single(halo, owned_coords.index_select(0, send_idx).contiguous(), recv_splits, splits,
-                           group=group)
-    return HaloPlan(rank, world, n, send_idx, splits, recv_splits, halo)
+    local = owned_coords.index_select(0, order)
+    dist.all_to_all_single(halo, local.index_select(0, send_idx).contiguous(), recv_splits, splits, group=group)
+    return HaloPlan(rank, world, n, n_interior, order, send_idx, splits, recv_splits, halo)
+
+
+def owned_local(plan, t):
+    """Rows of a tensor over the caller's owned rows, in the plan's local order."""
+    return t.index_select(0, plan.order)
 
 
 def local_coords(plan, owned_coords):
-    """Coords of the local input rows: owned rows, then halo rows."""
-    return torch.cat([owned_coords, plan.halo_coords], 0).contiguous()
+    """Coords of the local input rows: owned rows (plan order), then halo rows."""
+    return torch.cat([owned_local(plan, owned_coords), plan.halo_coords], 0).contiguous()
 
 
-def exchange_halo(plan, owned_feats, out=None, group=None):
+def exchange_halo(plan, owned_feats, out=None, group=None, async_op=False):
     """Collective: returns (n_own + n_halo, C) features, owned rows first then halo rows.
 
-    `out`, when given, must already hold the owned rows in its first n_own rows
-    (e.g. the previous layer wrote them there); only the halo rows are filled.
+    ``owned_feats`` holds the owned rows in plan order.  ``out``, when given,
+    must already hold them in its first n_own rows (e.g. the previous layer
+    wrote them there); only the halo rows are filled.  With ``async_op`` the
+    call returns ``(out, work)`` as soon as the exchange is enqueued (NCCL runs
+    it beside work queued later on the current stream) and ``work.wait()``
+    orders the current stream after it.
     """
     import torch.distributed as dist
     c = owned_feats.shape[1]
@@ -136,5 +157,6 @@ def exchange_halo(plan, owned_feats, out=None, group=None):
         out = torch.empty((plan.n_own + plan.n_halo, c), dtype=owned_feats.dtype, device=owned_feats.device)
         out[:plan.n_own].copy_(owned_feats)
     send = owned_feats.index_select(0, plan.send_idx).contiguous()
-    dist.all_to_all_single(out[plan.n_own:], send, plan.recv_splits, plan.send_splits, group=group)
-    return out
+    work = dist.all_to_all_single(out[plan.n_own:], send, plan.recv_splits, plan.send_splits, group=group,
+                                  async_op=async_op)
+    return (out, work) if async_op else out

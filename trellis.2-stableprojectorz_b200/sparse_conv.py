@@ -67,6 +67,10 @@ class Engine:
     def check(self, status, what=""):
         L.check(status, self.handle, what)
 
+    def set_conv_ctas(self, max_ctas=0):
+        """CTAs of the persistent conv (0 = one per SM); fewer leave SMs for a concurrent collective."""
+        self.check(self.lib.sc_set_conv_ctas(self.handle, int(max_ctas)), "sc_set_conv_ctas")
+
     def launch_count(self):
         """Kernels launched through this handle so far."""
         return int(self.lib.sc_launch_count(self.handle))
@@ -160,25 +164,28 @@ def _flags(tile_sort, check):
     return f if check else f | L.SC_BUILD_DEFER_CHECK
 
 
-def build_kmap(coords, dilation=1, engine=None, tile_sort=True, check=True, n_out=None):
+def build_kmap(coords, dilation=1, engine=None, tile_sort=True, check=True, n_out=None, out_begin=0):
     """Submanifold 3x3x3 neighbour map (``sc_kmap_build``).
 
-    With ``n_out`` only the first ``n_out`` rows are outputs while neighbours
-    are looked up among all rows (``sc_kmap_build_ex``; sharded convs put a
-    rank's owned voxels first and its halo after them).
+    With ``n_out`` / ``out_begin`` only rows ``[out_begin, out_begin + n_out)``
+    are outputs (map row j is input row ``out_begin + j``) while neighbours are
+    looked up among all rows (``sc_kmap_build_range``; sharded convs order a
+    rank's owned voxels interior first, then boundary, then its halo).
     """
     coords = _coords_arg(coords)
     eng = engine or get_engine(coords.device)
     eng.bind_stream()
     p = ctypes.c_void_p()
     n = coords.shape[0]
-    if n_out is None:
+    if n_out is None and out_begin == 0:
         eng.check(eng.lib.sc_kmap_build(eng.handle, _ptr(coords), n, 3, int(dilation),
                                         _flags(tile_sort, check), ctypes.byref(p)), "sc_kmap_build")
         n_out = n
     else:
-        eng.check(eng.lib.sc_kmap_build_ex(eng.handle, _ptr(coords), n, int(n_out), 3, int(dilation),
-                                           _flags(tile_sort, check), ctypes.byref(p)), "sc_kmap_build_ex")
+        n_out = n - int(out_begin) if n_out is None else int(n_out)
+        eng.check(eng.lib.sc_kmap_build_range(eng.handle, _ptr(coords), n, int(out_begin), int(out_begin) + n_out, 3,
+                                              int(dilation), _flags(tile_sort, check), ctypes.byref(p)),
+                  "sc_kmap_build_range")
     return KernelMap(eng, p, L.SC_KMAP_SUBM, n, n_out, 27)
 
 
