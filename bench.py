@@ -580,7 +580,8 @@ def run_table(args):
         flops = sum(2.0 * ci * co * inf["num_pairs"] for (ci, co), inf in zip(chans, infos))
         gm, gc = statistics.median(t_map), statistics.median(t_conv)
         del maps
-        cpu_s, cpu_pairs, cpu_n = _cpu_chain(idx, w, 400_000)
+        cpu_runs = [_cpu_chain(idx, w, 400_000) for _ in range(2 + 5)][2:]  # 2 warm-ups, median of 5
+        cpu_s, cpu_n = statistics.median(r[0] for r in cpu_runs), cpu_runs[0][2]
         cpu_full_ms = 1e3 * cpu_s * (w.n / cpu_n)
         line = {
             "table": w.name, "voxels": w.n, "pairs": [inf["num_pairs"] for inf in infos],
@@ -589,7 +590,7 @@ def run_table(args):
             "conv_pct_of_bf16_peak": 100.0 * flops / (gc * 1e-3) / 1e12 / float(peaks["bf16_tflops"]),
             "peak_source": f"{peak_src} bf16_tflops (burst)",
             "gpu_voxels_per_s": w.n / ((gm + gc) * 1e-3),
-            "cpu_ms": cpu_full_ms, "cpu_threads": torch.get_num_threads(),
+            "cpu_ms": cpu_full_ms, "cpu_threads": torch.get_num_threads(), "cpu_runs": "median of 5 after 2 warm-ups",
             "cpu_sample": ("full workload" if cpu_n == w.n else
                            f"first {cpu_n} Morton-ordered voxels, time scaled by {w.n / cpu_n:.2f}"),
             "speedup_vs_cpu": cpu_full_ms / (gm + gc), "steps": steps,
