@@ -566,7 +566,12 @@ sc_status launch_tc(Handle* h, const KMap* km, const void* feats, const void* we
   // Work order balances CTAs that run few items (10 per CTA on the 256^3
   // workload: -9% conv time); with many items per CTA static striding is
   // already balanced and the natural tile order keeps better L2 locality.
-  p.group_order = p.num_items < kWorkOrderMaxItemsPerCta * grid ? km->group_order[TPI - 1] : nullptr;
+  p.group_order = nullptr;
+  if (p.num_items < kWorkOrderMaxItemsPerCta * grid) {
+    const sc_status st = ensure_group_order(h, km, TPI);
+    if (st != SC_OK) return st;
+    p.group_order = km->group_order[TPI - 1];
+  }
   ++h->launches;
   kern<<<static_cast<unsigned>(grid), kTcThreads, S::kSmemBytes, h->stream>>>(tb, p);
   e = cudaGetLastError();

@@ -41,7 +41,9 @@ struct KMap {
   uint32_t* tile_mask = nullptr;
   // Groups of TPI = 1, 2 consecutive tiles ordered by descending work (number
   // of offsets the group runs); the conv schedules its items in this order.
-  int32_t* group_order[2] = {nullptr, nullptr};
+  // Filled on first use by a conv that needs it (ensure_group_order).
+  mutable int32_t* group_order[2] = {nullptr, nullptr};
+  mutable bool group_order_ready[2] = {false, false};
   int32_t* out_coords = nullptr;   // down-sample: parent coords [n_out, 4]
   int32_t* parent_of = nullptr;    // down-sample: parent of every fine row [n_in]
   unsigned long long* counters = nullptr;  // [0] valid pairs, [1] tile pairs
@@ -59,6 +61,7 @@ sc_status build_down2(Handle* h, const int32_t* coords, int64_t n, uint32_t flag
 sc_status build_up2(Handle* h, const KMap* down, uint32_t flags, KMap** out);
 sc_status export_map(Handle* h, const KMap* km, int32_t* map_out);
 // allocation-free map build into caller memory (sc_noalloc.cu)
+sc_status ensure_group_order(Handle* h, const KMap* km, int tpi);
 sc_status build_subm_noalloc(Handle* h, const int32_t* coords, int64_t n, int dilation, int32_t* map_out);
 void free_kmap(Handle* h, KMap* km);
 
