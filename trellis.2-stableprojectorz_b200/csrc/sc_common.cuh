@@ -71,6 +71,24 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
     }
   }
 }
+// Bounded wait with exponential __nanosleep backoff (from 32 ns up to
+// kMaxSleepNs) between polls, so a waiting warp does not take issue slots from
+// the warps doing the work on the same SM sub-partition.
+template <unsigned kMaxSleepNs = 1024>
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  unsigned ns = 32;
+  for (;;) {
+    __nanosleep(ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (ns < kMaxSleepNs) ns <<= 1;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_error(err, SC_ETIMEOUT);
+      return false;
+    }
+  }
+}
 
 // ---------------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {

@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t d_tmem = tmem_base + acc * static_cast<uint32_t>(S::kAccCols);
         const int nsteps = __popc(group_mask(g)) * p.nchunks;
         for (int s = 0; s < nsteps; ++s) {
-          if (!mbar_wait(full0 + 8u * stage, phase, p.err)) {
+          if (!mbar_wait_sleep<64>(full0 + 8u * stage, phase, p.err)) {
             ok = false;
             break;
           }
@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int64_t g = item_group(item, cb);
       const uint32_t acc = it & 1u, aph = (it >> 1) & 1u;
       int w = 1;
-      if (lane == 0) w = mbar_wait(tfull0 + 8u * acc, aph, p.err) ? 1 : 0;
+      if (lane == 0) w = mbar_wait_sleep(tfull0 + 8u * acc, aph, p.err) ? 1 : 0;
       w = __shfl_sync(0xffffffffu, w, 0);
       if (!w) break;
       tc_fence_after();
