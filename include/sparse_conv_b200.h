@@ -65,7 +65,10 @@ enum { SC_KMAP_SUBM = 0, SC_KMAP_DOWN2 = 1, SC_KMAP_UP2 = 2 };
 /* build flags */
 enum {
   SC_BUILD_NO_TILE_SORT = 1u, /* keep output order for tiles (no mask sort) */
-  SC_BUILD_DEFER_CHECK = 2u   /* do not wait for the device error word */
+  SC_BUILD_DEFER_CHECK = 2u,  /* do not wait for the device error word */
+  SC_BUILD_HALO = 4u          /* submanifold maps: tiles in output order plus per-tile
+                                 halo lists for the halo-staged conv (waits once to read
+                                 the largest halo) */
 };
 /* conv epilogue flags, applied in this order: +bias, LayerNorm, SiLU, +residual */
 enum { SC_EPI_SILU = 1u, SC_EPI_RESIDUAL = 2u, SC_EPI_LAYERNORM = 4u };
@@ -85,6 +88,7 @@ typedef struct sc_kmap_info {
   int64_t num_pairs;     /* M: valid (output, offset) pairs */
   int64_t num_tiles;     /* 128-row output tiles */
   int64_t tile_pairs;    /* sum over tiles of 128 * popcount(tile offset mask) */
+  int64_t halo_max;      /* largest per-tile halo of an SC_BUILD_HALO map, else -1 */
 } sc_kmap_info;
 
 typedef struct sc_handle sc_handle;

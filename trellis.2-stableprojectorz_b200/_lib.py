@@ -26,7 +26,7 @@ SC_F32, SC_BF16, SC_F16 = 0, 1, 2
 # map modes / kinds / flags
 SC_MAP_HASH, SC_MAP_SORT = 0, 1
 SC_KMAP_SUBM, SC_KMAP_DOWN2, SC_KMAP_UP2 = 0, 1, 2
-SC_BUILD_NO_TILE_SORT, SC_BUILD_DEFER_CHECK = 1, 2
+SC_BUILD_NO_TILE_SORT, SC_BUILD_DEFER_CHECK, SC_BUILD_HALO = 1, 2, 4
 SC_EPI_SILU, SC_EPI_RESIDUAL, SC_EPI_LAYERNORM = 1, 2, 4
 SC_NOALLOC_MAX_VOXELS = 131072
 
@@ -55,7 +55,8 @@ class ScConfig(ctypes.Structure):
 class ScKmapInfo(ctypes.Structure):
     _fields_ = [("kind", ctypes.c_int32), ("kernel_volume", ctypes.c_int32), ("n_in", ctypes.c_int64),
                 ("n_out", ctypes.c_int64), ("num_pairs", ctypes.c_int64), ("num_tiles", ctypes.c_int64),
-                ("tile_pairs", ctypes.c_int64)]
+                ("tile_pairs", ctypes.c_int64),
+                ("halo_max", ctypes.c_int64)]
 
 
 _P = ctypes.c_void_p

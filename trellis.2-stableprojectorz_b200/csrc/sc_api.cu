@@ -293,7 +293,7 @@ sc_status sc_kmap_get_info(sc_handle* h, const sc_kmap* km, sc_kmap_info* info) 
   if (!h || !km || !info) return SC_EINVAL;
   Handle* H = &h->impl;
   sc::DeviceGuard g(H->device);
-  unsigned long long c[2] = {0, 0};
+  unsigned long long c[3] = {0, 0, 0};
   cudaError_t e = cudaMemcpyAsync(c, km->impl->counters, sizeof(c), cudaMemcpyDeviceToHost, H->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(H->stream);
   if (e != cudaSuccess) return sc::cuda_error(H, e, "kmap info");
@@ -304,6 +304,7 @@ sc_status sc_kmap_get_info(sc_handle* h, const sc_kmap* km, sc_kmap_info* info) 
   info->num_pairs = static_cast<int64_t>(c[0]);
   info->num_tiles = km->impl->num_tiles;
   info->tile_pairs = static_cast<int64_t>(c[1]);
+  info->halo_max = km->impl->lidx ? static_cast<int64_t>(c[2]) : -1;
   return SC_OK;
 }
 

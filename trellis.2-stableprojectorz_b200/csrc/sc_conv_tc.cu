@@ -348,22 +348,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int64_t round_next = round + 1;
       const int64_t next = next_item(round_next);
       const int nact_next = next >= 0 ? load_idx(next) : 0;
-      uint32_t mask = group_mask(g);
-      for (int j = 0; mask; ++j) {
-        const int v = __ffs(mask) - 1;
-        mask &= mask - 1;
-        // One shared load per tile: lane l reads the index of row
-        // RW*w + l%RW + (l/RW)*RSTEP, which is row row0 + c*RSTEP of the thread
-        // at lane c*RW + l/CPR; shuffles hand every thread its CPR rows.
-        constexpr int RW = 32 / CPR;
-        int rows_idx[TPI][CPR];
+      // K chunks outermost, offsets inside: every output row accumulates
+      // (chunk, offset) products in the same order in every conv kernel.
+      const uint32_t mask0 = group_mask(g);
+      for (int kc = 0; kc < p.nchunks; ++kc) {
+        uint32_t mask = mask0;
+        for (int j = 0; mask; ++j) {
+          const int v = __ffs(mask) - 1;
+          mask &= mask - 1;
+          // One shared load per tile: lane l reads the index of row
+          // RW*w + l%RW + (l/RW)*RSTEP, which is row row0 + c*RSTEP of the
+          // thread at lane c*RW + l/CPR; shuffles hand every thread its rows.
+          constexpr int RW = 32 / CPR;
+          int rows_idx[TPI][CPR];
 #pragma unroll
-        for (int i = 0; i < TPI; ++i) {
-          const int mine = idx_s[(j * TPI + i) * 128 + RW * warp + (lane % RW) + (lane / RW) * RSTEP];
+          for (int i = 0; i < TPI; ++i) {
+            const int mine = idx_s[(j * TPI + i) * 128 + RW * warp + (lane % RW) + (lane / RW) * RSTEP];
 #pragma unroll
-          for (int c = 0; c < CPR; ++c) rows_idx[i][c] = __shfl_sync(0xffffffffu, mine, c * RW + lane / CPR);
-        }
-        for (int kc = 0; kc < p.nchunks; ++kc) {
+            for (int c = 0; c < CPR; ++c) rows_idx[i][c] = __shfl_sync(0xffffffffu, mine, c * RW + lane / CPR);
+          }
           int w = 0;
           if (lane == 0 && !abort) w = mbar_wait(empty0 + 8u * stage, phase ^ 1u, p.err) ? 1 : 0;
           if (!__all_sync(0xffffffffu, lane != 0 || w != 0)) {
@@ -516,6 +519,395 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ------------------------------------------------------- halo-staged conv
+// For maps built with SC_BUILD_HALO (tiles = 128 consecutive output rows).
+// A Morton-ordered tile's 27 x 128 gathers read only a few hundred distinct
+// input rows (245 on average on the 256^3 shell workload, against 1,958
+// gathered rows), so each tile's distinct rows are staged in shared memory
+// once per 64-channel chunk by TMA row gathers, and the A operand of every
+// offset is assembled from that halo straight into tensor memory:
+//   warps 0-7  A builders in two groups of four (warp w writes TMEM lanes
+//              32*(w%4)..+31); group g takes the (chunk, offset) steps with
+//              step % 2 == g: each lane copies its row's 64 channels from
+//              the halo (or zeros) into TMEM with tcgen05.st
+//   warp 8     TMEM allocator + single-thread MMA issuer (A from TMEM, weight
+//              tile B from shared memory)
+//   warps 9-12 epilogue (as in conv_tc_kernel)
+//   warp 13    TMA: per tile the 6.9 KB position block, per chunk the halo
+//   warp 14    TMA: weight tiles per (chunk, offset)
+// Products are accumulated chunk by chunk and offset by offset, the same order
+// as conv_tc_kernel, so both kernels give identical results.
+constexpr int kHaloKernelThreads = 480;
+constexpr int kHaloMmaWarp = 8, kHaloEpiWarp0 = 9, kHaloTmaWarp = 13;
+constexpr int kHaloBStages = 6;
+constexpr int kHaloASlots = 8;
+constexpr int kHaloSlotBytes = kHaloCap * 128;
+constexpr int kLidxBytes = 27 * 128 * 2;
+constexpr int kHaloBarBytes = 512;
+constexpr int kHaloSmemBytes = 2 * kHaloSlotBytes + kHaloBStages * 16384 + 2 * kLidxBytes + 4096 + kHaloBarBytes + 1024;
+static_assert(kHaloSmemBytes <= 227 * 1024, "halo conv shared memory plan too large");
+constexpr uint32_t kHaloAccCols = 128, kHaloACol0 = 256, kHaloTmemCols = 512;
+
+struct HaloConvParams {
+  const void* feats;
+  const int32_t* gidx;
+  const int32_t* halo_rows;
+  const int32_t* halo_n;
+  const uint16_t* lidx;
+  const int32_t* tile_rows;
+  const uint32_t* tile_mask;
+  const int32_t* group_order;
+  const void* bias;
+  const void* residual;
+  void* out;
+  int64_t num_tiles;
+  int ci;
+  int co;
+  int nchunks;
+  uint32_t epi;
+  float eps;
+  int* err;
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(kHaloKernelThreads, 1)
+    conv_halo_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmF,
+                     const HaloConvParams p) {
+  using T = std::conditional_t<BF16, __nv_bfloat16, __half>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* halo_s = smem;                                              // [2][kHaloCap rows][128 B], 128B-swizzled
+  uint8_t* b_s = halo_s + 2 * kHaloSlotBytes;                          // [kHaloBStages][co rows][128 B]
+  uint16_t* lidx_s = reinterpret_cast<uint16_t*>(b_s + kHaloBStages * 16384);  // [2][27][128]
+  uint8_t* out_s = reinterpret_cast<uint8_t*>(lidx_s) + 2 * kLidxBytes;       // [4 warps][32 rows][16 cols]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(out_s + 4096);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 42);
+  static_assert((2 * 4 + 2 * kHaloBStages + 2 * kHaloASlots + 5) * 8 + 8 <= kHaloBarBytes, "barrier area");
+  const uint32_t bar0 = smem_u32(bars);
+  const uint32_t hfull0 = bar0, hempty0 = bar0 + 16, lfull0 = bar0 + 32, lempty0 = bar0 + 48;
+  const uint32_t bfull0 = bar0 + 64, bempty0 = bfull0 + 8 * kHaloBStages;
+  const uint32_t afull0 = bempty0 + 8 * kHaloBStages, aempty0 = afull0 + 8 * kHaloASlots;
+  const uint32_t tfull0 = aempty0 + 8 * kHaloASlots, tempty0 = tfull0 + 16, done_bar = tfull0 + 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int co = p.co;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(hfull0 + 8u * s, 1);
+      mbar_init(hempty0 + 8u * s, 8);
+      mbar_init(lfull0 + 8u * s, 1);
+      mbar_init(lempty0 + 8u * s, 8);
+      mbar_init(tfull0 + 8u * s, 1);
+      mbar_init(tempty0 + 8u * s, 128);
+    }
+    for (int s = 0; s < kHaloBStages; ++s) {
+      mbar_init(bfull0 + 8u * s, 1);
+      mbar_init(bempty0 + 8u * s, 1);
+    }
+    for (int s = 0; s < kHaloASlots; ++s) {
+      mbar_init(afull0 + 8u * s, 4);
+      mbar_init(aempty0 + 8u * s, 1);
+    }
+    mbar_init(done_bar, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tmB);
+    prefetch_tmap(&tmF);
+  }
+  if (warp == kHaloMmaWarp) {
+    tmem_alloc(smem_u32(s_tmem), kHaloTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+  // Item sequence: same serpentine rounds over the work order as conv_tc_kernel.
+  auto next_item = [&](int64_t& r) -> int64_t {
+    for (;; ++r) {
+      if (r * static_cast<int64_t>(gridDim.x) >= p.num_tiles) return -1;
+      const int64_t pos = (r & 1) ? static_cast<int64_t>(gridDim.x) - 1 - blockIdx.x : blockIdx.x;
+      const int64_t j = r * static_cast<int64_t>(gridDim.x) + pos;
+      if (j < p.num_tiles) return j;
+    }
+  };
+  auto tile_of = [&](int64_t j) -> int64_t {
+    return p.group_order ? static_cast<int64_t>(__ldg(p.group_order + j)) : j;
+  };
+
+  if (warp < 8) {
+    // ------------------------------------------------------- A builders
+    const int q = warp & 3, grp = warp >> 2;
+    uint32_t lph = 0, hph = 0;
+    int ls = 0, hs = 0;
+    uint32_t step = 0;  // (chunk, offset) steps of this CTA so far, both groups
+    bool ok = true;
+    auto wait_all = [&](uint32_t bar, uint32_t par) {
+      int w = 1;
+      if (lane == 0) w = mbar_wait(bar, par, p.err) ? 1 : 0;
+      w = __shfl_sync(0xffffffffu, w, 0);
+      return w != 0;
+    };
+    int64_t round = 0;
+    for (int64_t j = next_item(round); ok && j >= 0; ++round, j = next_item(round)) {
+      const int64_t t = tile_of(j);
+      const uint32_t mask0 = __ldg(p.tile_mask + t);
+      // tiles with more distinct rows than a halo slot holds read their rows
+      // straight from global memory (these threads issue no async copies)
+      const bool direct = __ldg(p.halo_n + t) > kHaloCap;
+      if (!wait_all(lfull0 + 8u * ls, lph)) { ok = false; break; }
+      const uint16_t* lrow = lidx_s + ls * (27 * 128) + q * 32 + lane;
+      const int32_t* grow = p.gidx + t * 27 * 128 + q * 32 + lane;
+      for (int kc = 0; ok && kc < p.nchunks; ++kc) {
+        if (!wait_all(hfull0 + 8u * hs, hph)) { ok = false; break; }
+        const uint32_t hbase = smem_u32(halo_s + hs * kHaloSlotBytes);
+        uint32_t mask = mask0;
+        while (mask) {
+          const int v = __ffs(mask) - 1;
+          mask &= mask - 1u;
+          const uint32_t my = step++;
+          if ((my & 1u) != static_cast<uint32_t>(grp)) continue;
+          const uint32_t as = my % kHaloASlots, aph = (my / kHaloASlots) & 1u;
+          if (!wait_all(aempty0 + 8u * as, aph ^ 1u)) { ok = false; break; }
+          tc_fence_after();
+          uint32_t val[32];
+          if (direct) {
+            const int r = __ldg(grow + v * 128);
+            if (r >= 0) {
+              const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.feats) +
+                                                                static_cast<int64_t>(r) * p.ci + kc * 64);
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                const uint4 u = __ldg(src + c);
+                val[4 * c] = u.x;
+                val[4 * c + 1] = u.y;
+                val[4 * c + 2] = u.z;
+                val[4 * c + 3] = u.w;
+              }
+            } else {
+#pragma unroll
+              for (int c = 0; c < 32; ++c) val[c] = 0u;
+            }
+          } else if (const uint32_t l = lrow[v * 128]; l != 0xFFFFu) {
+            const uint32_t rb = hbase + l * 128u;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              uint32_t a, b, cc, d;
+              asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(a), "=r"(b), "=r"(cc), "=r"(d)
+                           : "r"(rb + ((static_cast<uint32_t>(c) ^ (l & 7u)) << 4)));
+              val[4 * c] = a;
+              val[4 * c + 1] = b;
+              val[4 * c + 2] = cc;
+              val[4 * c + 3] = d;
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) val[c] = 0u;
+          }
+          tmem_st32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + kHaloACol0 + as * 32u, val);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(afull0 + 8u * as);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(hempty0 + 8u * hs);
+        if (++hs == 2) {
+          hs = 0;
+          hph ^= 1u;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(lempty0 + 8u * ls);
+      if (++ls == 2) {
+        ls = 0;
+        lph ^= 1u;
+      }
+    }
+  } else if (warp == kHaloMmaWarp) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(128, co, BF16);
+      int bs = 0, as = 0;
+      uint32_t bph = 0, aph = 0, it = 0;
+      bool ok = true;
+      int64_t round = 0;
+      for (int64_t j = next_item(round); ok && j >= 0; ++round, j = next_item(round), ++it) {
+        const int64_t t = tile_of(j);
+        const uint32_t mask0 = __ldg(p.tile_mask + t);
+        const uint32_t acc = it & 1u, tph = (it >> 1) & 1u;
+        if (!mbar_wait(tempty0 + 8u * acc, tph ^ 1u, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kHaloAccCols;
+        bool first = true;
+        for (int kc = 0; ok && kc < p.nchunks; ++kc) {
+          uint32_t mask = mask0;
+          while (mask) {
+            mask &= mask - 1u;
+            if (!mbar_wait_sleep<64>(afull0 + 8u * as, aph, p.err) || !mbar_wait(bfull0 + 8u * bs, bph, p.err)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t b0 = smem_u32(b_s + bs * 16384);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              tc_mma_f16_tmem_a(d_tmem, tmem_base + kHaloACol0 + as * 32u + 8u * k, smem_desc(b0 + 32u * k, 1024, 2),
+                                idesc, (first && k == 0) ? 0u : 1u);
+            first = false;
+            tc_commit(aempty0 + 8u * as);
+            tc_commit(bempty0 + 8u * bs);
+            if (++as == kHaloASlots) {
+              as = 0;
+              aph ^= 1u;
+            }
+            if (++bs == kHaloBStages) {
+              bs = 0;
+              bph ^= 1u;
+            }
+          }
+        }
+        if (!ok) break;
+        tc_commit(tfull0 + 8u * acc);
+      }
+      tc_commit(done_bar);
+      mbar_wait(done_bar, 0, p.err);
+    }
+    __syncwarp();
+  } else if (warp < kHaloTmaWarp) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const T* bias = static_cast<const T*>(p.bias);
+    const T* res = static_cast<const T*>(p.residual);
+    T* out = static_cast<T*>(p.out);
+    uint8_t* wbuf = out_s + (warp - kHaloEpiWarp0) * (32 * 32);
+    uint32_t it = 0;
+    int64_t round = 0;
+    for (int64_t j = next_item(round); j >= 0; ++round, j = next_item(round), ++it) {
+      const int64_t t = tile_of(j);
+      const uint32_t acc = it & 1u, aph = (it >> 1) & 1u;
+      int w = 1;
+      if (lane == 0) w = mbar_wait_sleep(tfull0 + 8u * acc, aph, p.err) ? 1 : 0;
+      w = __shfl_sync(0xffffffffu, w, 0);
+      if (!w) break;
+      tc_fence_after();
+      const bool live = __ldg(p.tile_mask + t) != 0u;
+      const int bn32 = co & ~31;
+      const int r = __ldg(p.tile_rows + t * 128 + row);
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kHaloAccCols;
+      float mean = 0.f, rstd = 1.f;
+      if (p.epi & SC_EPI_LAYERNORM) {
+        float s1 = 0.f;
+        for (int c0 = 0; c0 < bn32; c0 += 32) s1 += chunk_sum<T, 32>(tb, c0, live, bias, 0, 0.f, false);
+        if (bn32 < co) s1 += chunk_sum<T, 16>(tb, bn32, live, bias, 0, 0.f, false);
+        mean = s1 / static_cast<float>(co);
+        float s2 = 0.f;
+        for (int c0 = 0; c0 < bn32; c0 += 32) s2 += chunk_sum<T, 32>(tb, c0, live, bias, 0, mean, true);
+        if (bn32 < co) s2 += chunk_sum<T, 16>(tb, bn32, live, bias, 0, mean, true);
+        rstd = rsqrtf(s2 / static_cast<float>(co) + p.eps);
+      }
+      for (int c0 = 0; c0 < bn32; c0 += 32)
+        epi_chunk<T, 32>(tb, c0, live, bias, res, out, r, co, 0, mean, rstd, p.epi, wbuf, lane);
+      if (bn32 < co) epi_chunk<T, 16>(tb, bn32, live, bias, res, out, r, co, 0, mean, rstd, p.epi, wbuf, lane);
+      tc_fence_before();
+      mbar_arrive(tempty0 + 8u * acc);
+      __syncwarp();
+    }
+  } else if (warp == kHaloTmaWarp) {
+    // ------------------------------------------ TMA: positions and halos
+    if (lane == 0) {
+      int ls = 0, hs = 0;
+      uint32_t lph = 0, hph = 0;
+      uint32_t lused = 0, lpar = 0, hused = 0, hpar = 0;  // slots with a copy issued, parity of the last one
+      bool ok = true;
+      int64_t round = 0;
+      for (int64_t j = next_item(round); ok && j >= 0; ++round, j = next_item(round)) {
+        const int64_t t = tile_of(j);
+        if (!mbar_wait(lempty0 + 8u * ls, lph ^ 1u, p.err)) break;
+        const uint32_t lbar = lfull0 + 8u * ls;
+        mbar_arrive_expect_tx(lbar, kLidxBytes);
+        bulk_load(smem_u32(lidx_s + ls * (27 * 128)), p.lidx + t * (27 * 128), kLidxBytes, lbar);
+        lused |= 1u << ls;
+        lpar = (lpar & ~(1u << ls)) | (lph << ls);
+        if (++ls == 2) {
+          ls = 0;
+          lph ^= 1u;
+        }
+        const int hn_all = __ldg(p.halo_n + t);
+        const int groups = hn_all > kHaloCap ? 0 : (hn_all + 3) >> 2;  // direct tiles stage nothing
+        const int4* hrows = reinterpret_cast<const int4*>(p.halo_rows + t * kHaloCap);
+        for (int kc = 0; kc < p.nchunks; ++kc) {
+          if (!mbar_wait(hempty0 + 8u * hs, hph ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          const uint32_t hbar = hfull0 + 8u * hs;
+          const uint32_t hdst = smem_u32(halo_s + hs * kHaloSlotBytes);
+          mbar_arrive_expect_tx(hbar, static_cast<uint32_t>(groups) * 512u);
+          for (int g4 = 0; g4 < groups; ++g4) {
+            const int4 r4 = __ldg(hrows + g4);
+            tma_gather4(hdst + g4 * 512u, &tmF, kc * 64, r4.x, r4.y, r4.z, r4.w, hbar);
+          }
+          hused |= 1u << hs;
+          hpar = (hpar & ~(1u << hs)) | (hph << hs);
+          if (++hs == 2) {
+            hs = 0;
+            hph ^= 1u;
+          }
+        }
+      }
+      // Let every copy issued into this CTA's shared memory land before exit.
+      for (int s = 0; s < 2; ++s) {
+        if (lused & (1u << s)) mbar_wait(lfull0 + 8u * s, (lpar >> s) & 1u, nullptr);
+        if (hused & (1u << s)) mbar_wait(hfull0 + 8u * s, (hpar >> s) & 1u, nullptr);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------- TMA: weight tiles
+    if (lane == 0) {
+      int bs = 0;
+      uint32_t bph = 0, bused = 0, bpar = 0;
+      bool ok = true;
+      const uint32_t b_tx = static_cast<uint32_t>(co) * 128u;
+      int64_t round = 0;
+      for (int64_t j = next_item(round); ok && j >= 0; ++round, j = next_item(round)) {
+        const int64_t t = tile_of(j);
+        const uint32_t mask0 = __ldg(p.tile_mask + t);
+        for (int kc = 0; ok && kc < p.nchunks; ++kc) {
+          uint32_t mask = mask0;
+          while (mask) {
+            const int v = __ffs(mask) - 1;
+            mask &= mask - 1u;
+            if (!mbar_wait(bempty0 + 8u * bs, bph ^ 1u, p.err)) {
+              ok = false;
+              break;
+            }
+            const uint32_t bbar = bfull0 + 8u * bs;
+            mbar_arrive_expect_tx(bbar, b_tx);
+            tma_load_2d(smem_u32(b_s + bs * 16384), &tmB, v * p.ci + kc * 64, 0, bbar);
+            bused |= 1u << bs;
+            bpar = (bpar & ~(1u << bs)) | (bph << bs);
+            if (++bs == kHaloBStages) {
+              bs = 0;
+              bph ^= 1u;
+            }
+          }
+        }
+      }
+      for (int s = 0; s < kHaloBStages; ++s)
+        if (bused & (1u << s)) mbar_wait(bfull0 + 8u * s, (bpar >> s) & 1u, nullptr);
+    }
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kHaloMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kHaloTmemCols);
+  }
+}
+
 // --------------------------------------------------------------- host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -634,6 +1026,56 @@ sc_status check_gather_bounds(Handle* h, const KMap* km) {
   return SC_OK;
 }
 
+
+template <bool BF16>
+sc_status launch_halo(Handle* h, const KMap* km, const void* feats, const void* weight, const void* bias,
+                      const void* residual, void* out, int ci, int co, uint32_t epi, float eps) {
+  CUtensorMap tb, tf;
+  if (!make_map_2d(&tb, BF16, weight, static_cast<uint64_t>(km->K) * ci, co, static_cast<uint64_t>(km->K) * ci * 2,
+                   64, co, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map_2d(&tf, BF16, feats, ci, km->n_in, static_cast<uint64_t>(ci) * 2, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B))
+    return set_error(h, SC_ECUDA, "cuTensorMapEncodeTiled failed");
+  HaloConvParams p{};
+  p.feats = feats;
+  p.gidx = km->gidx;
+  p.halo_rows = km->halo_rows;
+  p.halo_n = km->halo_n;
+  p.lidx = km->lidx;
+  p.tile_rows = km->tile_rows;
+  p.tile_mask = km->tile_mask;
+  p.bias = bias;
+  p.residual = residual;
+  p.out = out;
+  p.num_tiles = km->num_tiles;
+  p.ci = ci;
+  p.co = co;
+  p.nchunks = ci / 64;
+  p.epi = epi;
+  p.eps = eps;
+  p.err = h->derr;
+  const int64_t ctas = h->conv_ctas > 0 ? std::min(h->conv_ctas, h->num_sms) : h->num_sms;
+  const int64_t grid = std::min<int64_t>(p.num_tiles, ctas);
+  if (p.num_tiles < kWorkOrderMaxItemsPerCta * grid) {
+    const sc_status st = ensure_group_order(h, km, 1);
+    if (st != SC_OK) return st;
+    p.group_order = km->group_order[0];
+  }
+  auto kern = conv_halo_kernel<BF16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kHaloSmemBytes);
+  if (e != cudaSuccess) return cuda_error(h, e, "halo conv smem attribute");
+  ++h->launches;
+  kern<<<static_cast<unsigned>(grid), kHaloKernelThreads, kHaloSmemBytes, h->stream>>>(tb, tf, p);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? SC_OK : cuda_error(h, e, "halo conv launch");
+}
+
+// The halo-staged kernel applies to submanifold maps built with halo data,
+// for Ci a multiple of 64 and Co <= 128.
+bool halo_applies(const Handle* h, const KMap* km, int ci, int co) {
+  return km->lidx && km->K == 27 && km->kind == SC_KMAP_SUBM &&
+         ci % 64 == 0 && co % 16 == 0 && co >= 16 && co <= 128 && !h->debug_bounds && km->num_tiles > 0;
+}
+
 sc_status conv_tc(Handle* h, const KMap* km, const void* feats, const void* weight, const void* bias,
                   const void* residual, void* out, int ci, int co, sc_dtype dtype, uint32_t epi, float eps) {
   if (ci % 16 != 0 || co % 16 != 0)
@@ -656,6 +1098,9 @@ sc_status conv_tc(Handle* h, const KMap* km, const void* feats, const void* weig
     const sc_status st = check_gather_bounds(h, km);
     if (st != SC_OK) return st;
   }
+  if (halo_applies(h, km, ci, co))
+    return dtype == SC_BF16 ? launch_halo<true>(h, km, feats, weight, bias, residual, out, ci, co, epi, eps)
+                            : launch_halo<false>(h, km, feats, weight, bias, residual, out, ci, co, epi, eps);
   TcParams p{};
   p.gidx = km->gidx;
   p.tile_rows = km->tile_rows;

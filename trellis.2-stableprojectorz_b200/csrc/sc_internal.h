@@ -30,6 +30,8 @@ struct Handle {
 //
 // Tiles are formed after sorting output rows by their K-bit neighbour mask
 // (stable), so rows of one tile share most of their offsets.
+constexpr int kHaloCap = 416;  // halo rows a tile may stage for the halo-staged conv
+
 struct KMap {
   int kind = SC_KMAP_SUBM;
   int K = 27;
@@ -44,6 +46,15 @@ struct KMap {
   // Filled on first use by a conv that needs it (ensure_group_order).
   mutable int32_t* group_order[2] = {nullptr, nullptr};
   mutable bool group_order_ready[2] = {false, false};
+  // Halo tiles (SC_BUILD_HALO): tiles are output rows in order; per tile the
+  // distinct input rows its gathers read (kHaloCap slots, padded with -1 to a
+  // multiple of 4) and per (tile, offset, slot) the position of the gathered
+  // row in that list (0xFFFF = no neighbour).  A tile with more than
+  // kHaloCap distinct rows is gathered straight from global memory by the
+  // halo conv.  The largest halo is kept in counters[2].
+  int32_t* halo_rows = nullptr;   // [num_tiles][kHaloCap]
+  int32_t* halo_n = nullptr;      // [num_tiles]
+  uint16_t* lidx = nullptr;       // [num_tiles][27][128]
   int32_t* out_coords = nullptr;   // down-sample: parent coords [n_out, 4]
   int32_t* parent_of = nullptr;    // down-sample: parent of every fine row [n_in]
   unsigned long long* counters = nullptr;  // [0] valid pairs, [1] tile pairs

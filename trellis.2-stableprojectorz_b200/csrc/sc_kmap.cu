@@ -585,6 +585,110 @@ __global__ void k_group_place(const uint32_t* __restrict__ tile_mask, int64_t nu
 }
 
 // Orders output rows by neighbour mask and writes gidx / tile_rows / tile_mask.
+
+// Halo lists of output-order tiles (one CTA per tile).  The 27 x 128 gathered
+// rows are deduplicated in a shared-memory hash set; the set is compacted into
+// the tile's halo list (order = slot order) and every gathered row is replaced
+// by its position in the list.  A tile's halo count above kHaloCap (or a full
+// set, which can only happen past the cap) marks it for direct gathers.
+constexpr int kHaloSlots = 1024;
+constexpr int kHaloThreads = 256;
+
+__device__ __forceinline__ uint32_t halo_hash(int r) {
+  return (static_cast<uint32_t>(r) * 0x9E3779B1u) >> (32 - 10);
+}
+
+__global__ void __launch_bounds__(kHaloThreads) k_build_halo(const int32_t* __restrict__ map, int64_t n_out,
+                                                             int32_t* __restrict__ halo_rows,
+                                                             int32_t* __restrict__ halo_n, uint16_t* __restrict__ lidx,
+                                                             unsigned long long* hmax) {
+  static_assert(kHaloSlots == 1 << 10, "halo_hash assumes 1024 slots");
+  __shared__ int tab[kHaloSlots];   // row or -1
+  __shared__ int pos[kHaloSlots];   // position in the halo list
+  __shared__ int s_warp[kHaloThreads / 32];
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x;
+  for (int e = tid; e < kHaloSlots; e += kHaloThreads) tab[e] = -1;
+  __syncthreads();
+  const int64_t base = t * kTileRows * 27;
+  const int64_t lim = (n_out - t * kTileRows) * 27;  // valid map entries of this tile
+  for (int e = tid; e < kTileRows * 27; e += kHaloThreads) {
+    const int r = e < lim ? map[base + e] : -1;
+    if (r < 0) continue;
+    uint32_t hh = halo_hash(r);
+    for (int probe = 0; probe < kHaloSlots; ++probe) {
+      const int old = atomicCAS(&tab[hh], -1, r);
+      if (old == -1 || old == r) break;
+      hh = (hh + 1) & (kHaloSlots - 1);
+    }
+  }
+  __syncthreads();
+  constexpr int kPer = kHaloSlots / kHaloThreads;
+  int cnt = 0;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) cnt += tab[tid * kPer + k] >= 0 ? 1 : 0;
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if ((tid & 31) >= o) incl += y;
+  }
+  if ((tid & 31) == 31) s_warp[tid >> 5] = incl;
+  __syncthreads();
+  int wbase = 0, total = 0;
+  for (int w = 0; w < kHaloThreads / 32; ++w) {
+    if (w < (tid >> 5)) wbase += s_warp[w];
+    total += s_warp[w];
+  }
+  // A full table may have dropped rows; it can only fill past the cap.
+  if (total >= kHaloSlots) total = kHaloSlots + 1;
+  int p = wbase + incl - cnt;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int sidx = tid * kPer + k;
+    const int r = tab[sidx];
+    if (r >= 0) {
+      pos[sidx] = p;
+      if (p < kHaloCap) halo_rows[t * kHaloCap + p] = r;
+      ++p;
+    }
+  }
+  // pad to a multiple of 4 rows (the conv gathers 4 rows per TMA instruction;
+  // row -1 reads zeros)
+  const int padded = min((total + 3) & ~3, kHaloCap);
+  for (int q = total + tid; q < padded; q += kHaloThreads) halo_rows[t * kHaloCap + q] = -1;
+  if (tid == 0) {
+    halo_n[t] = total;
+    atomicMax(hmax, static_cast<unsigned long long>(total));
+  }
+  if (total > kHaloCap) return;  // direct gathers: no positions needed
+  __syncthreads();
+  for (int e = tid; e < kTileRows * 27; e += kHaloThreads) {
+    const int v = e / kTileRows, i = e - v * kTileRows;
+    const int64_t ei = static_cast<int64_t>(i) * 27 + v;
+    const int r = ei < lim ? map[base + ei] : -1;
+    uint16_t l = 0xFFFFu;
+    if (r >= 0) {
+      uint32_t hh = halo_hash(r);
+      for (int probe = 0; probe < kHaloSlots && tab[hh] != r; ++probe) hh = (hh + 1) & (kHaloSlots - 1);
+      l = static_cast<uint16_t>(pos[hh]);
+    }
+    lidx[(t * 27 + v) * kTileRows + i] = l;
+  }
+}
+
+sc_status build_halo(Handle* h, KMap* km, const int32_t* map) {
+  const int64_t T = km->num_tiles;
+  SC_TRY_CUDA(dev_alloc(h, reinterpret_cast<void**>(&km->halo_rows), sizeof(int32_t) * T * kHaloCap), "alloc halo");
+  SC_TRY_CUDA(dev_alloc(h, reinterpret_cast<void**>(&km->halo_n), sizeof(int32_t) * T), "alloc halo");
+  SC_TRY_CUDA(dev_alloc(h, reinterpret_cast<void**>(&km->lidx), sizeof(uint16_t) * T * 27 * kTileRows), "alloc halo");
+  ++h->launches;
+  k_build_halo<<<static_cast<unsigned>(T), kHaloThreads, 0, h->stream>>>(map, km->n_out, km->halo_rows, km->halo_n,
+                                                                         km->lidx, km->counters + 2);
+  SC_TRY_CUDA(cudaGetLastError(), "halo launch");
+  return SC_OK;
+}
+
 sc_status finish_tiles(Handle* h, KMap* km, const int32_t* map, uint32_t* row_mask, uint32_t flags, Temps& tmp) {
   const int64_t n = km->n_out;
   if (n == 0) return SC_OK;
@@ -766,7 +870,9 @@ sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t out_be
     free_kmap(h, km);
     return cuda_error(h, e, "map build launch");
   }
-  st = finish_tiles(h, km, map, row_mask, flags, tmp);
+  const bool halo = (flags & SC_BUILD_HALO) != 0;
+  st = finish_tiles(h, km, map, row_mask, halo ? (flags | SC_BUILD_NO_TILE_SORT) : flags, tmp);
+  if (st == SC_OK && halo) st = build_halo(h, km, map);
   if (st != SC_OK) {
     free_kmap(h, km);
     return st;
@@ -928,6 +1034,9 @@ void free_kmap(Handle* h, KMap* km) {
   dev_free(h, km->gidx);
   dev_free(h, km->tile_rows);
   dev_free(h, km->tile_mask);
+  dev_free(h, km->halo_rows);
+  dev_free(h, km->halo_n);
+  dev_free(h, km->lidx);
   dev_free(h, km->group_order[0]);
   dev_free(h, km->group_order[1]);
   dev_free(h, km->out_coords);

@@ -159,18 +159,25 @@ def _coords_arg(coords):
     return coords.contiguous()
 
 
-def _flags(tile_sort, check):
+def _flags(tile_sort, check, halo=False):
     f = 0 if tile_sort else L.SC_BUILD_NO_TILE_SORT
+    if halo:
+        f |= L.SC_BUILD_HALO
     return f if check else f | L.SC_BUILD_DEFER_CHECK
 
 
-def build_kmap(coords, dilation=1, engine=None, tile_sort=True, check=True, n_out=None, out_begin=0):
+def build_kmap(coords, dilation=1, engine=None, tile_sort=True, check=True, n_out=None, out_begin=0, halo=False):
     """Submanifold 3x3x3 neighbour map (``sc_kmap_build``).
 
     With ``n_out`` / ``out_begin`` only rows ``[out_begin, out_begin + n_out)``
     are outputs (map row j is input row ``out_begin + j``) while neighbours are
     looked up among all rows (``sc_kmap_build_range``; sharded convs order a
     rank's owned voxels interior first, then boundary, then its halo).
+
+    ``halo=True`` (``SC_BUILD_HALO``) keeps tiles in row order and adds per-tile
+    halo lists, which lets bf16/f16 convs with Ci a multiple of 64 and Co <= 128
+    run the halo-staged kernel; it suits spatially ordered rows (Morton or
+    lexicographic).  The results equal those of the default map bit for bit.
     """
     coords = _coords_arg(coords)
     eng = engine or get_engine(coords.device)
@@ -179,12 +186,12 @@ def build_kmap(coords, dilation=1, engine=None, tile_sort=True, check=True, n_ou
     n = coords.shape[0]
     if n_out is None and out_begin == 0:
         eng.check(eng.lib.sc_kmap_build(eng.handle, _ptr(coords), n, 3, int(dilation),
-                                        _flags(tile_sort, check), ctypes.byref(p)), "sc_kmap_build")
+                                        _flags(tile_sort, check, halo), ctypes.byref(p)), "sc_kmap_build")
         n_out = n
     else:
         n_out = n - int(out_begin) if n_out is None else int(n_out)
         eng.check(eng.lib.sc_kmap_build_range(eng.handle, _ptr(coords), n, int(out_begin), int(out_begin) + n_out, 3,
-                                              int(dilation), _flags(tile_sort, check), ctypes.byref(p)),
+                                              int(dilation), _flags(tile_sort, check, halo), ctypes.byref(p)),
                   "sc_kmap_build_range")
     return KernelMap(eng, p, L.SC_KMAP_SUBM, n, n_out, 27)
 
