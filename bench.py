@@ -51,6 +51,9 @@ def parse_args():
                     help="c5 on >1 GPU: SMs left to NCCL while the interior conv runs beside the halo exchange; "
                          "-1 (default): exchange first, then one conv over all owned outputs (faster at 2 GPUs, "
                          "where the exchange is 0.04 ms)")
+    ap.add_argument("--c5-exchange", choices=["nccl", "peer"], default="peer",
+                    help="c5 on >1 GPU: halo exchange by the library's peer-memory push/wait kernels over NVLink "
+                         "(default) or by NCCL all_to_all_single")
     ap.add_argument("--workload", choices=["c2", "c5", "table"], default="c2",
                     help="c2: BASELINE configs[1] (default, data-parallel across ranks); "
                          "c5: configs[4] 1024^3 Morton-sharded across ranks with NCCL halo exchange (strong scaling)")
@@ -397,11 +400,19 @@ def run_c5(args):
     out = torch.empty((n_own, w.co), dtype=torch.bfloat16, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     reserve = args.c5_reserve_sms  # SMs left to the NCCL kernels while the interior conv runs
-    if plan is not None and reserve < 0:
+    peer = None
+    if plan is not None and (reserve < 0 or args.c5_exchange == "peer"):
         kms = [pkg.build_kmap(loc_c, n_out=n_own, engine=eng)]
+    if plan is not None and args.c5_exchange == "peer":
+        peer = S.PeerHaloExchange(plan, own_f, eng)
 
     def layer(ev=None):
         """Halo exchange beside the interior conv, then the boundary conv."""
+        if peer is not None:
+            loc = peer.exchange()
+            if ev: ev[1].record()
+            pkg.conv3d(kms[0], loc, weight, out=out)
+            return
         if plan is None or reserve < 0:
             if plan is not None:
                 S.exchange_halo(plan, buf[:n_own], out=buf)
@@ -435,8 +446,10 @@ def run_c5(args):
         torch.cuda.synchronize()
     launches = eng.launch_count() - launches0
     eng.synchronize()
+    if peer is not None:
+        peer.close()
     t_total = sum(e[0].elapsed_time(e[2]) for e in ev) / 1e3
-    t_first = sum(e[0].elapsed_time(e[1]) for e in ev) / 1e3  # exchange + interior conv (overlapped)
+    t_first = sum(e[0].elapsed_time(e[1]) for e in ev) / 1e3  # exchange (+ interior conv when overlapped)
     t_last = sum(e[1].elapsed_time(e[2]) for e in ev) / 1e3   # boundary conv
     per_rank = [t_total]
     if dist is not None:
@@ -465,7 +478,9 @@ def run_c5(args):
         "data": "synthetic: seeded union of 4 ellipsoid shells + 5% interior fill at 1024^3 (BASELINE configs[4])",
         "config": {"workload": w.name, "voxels": w.n, "ci": w.ci, "co": w.co, "pairs": pairs,
                    "halo_voxels_total": halo_total, "interior_voxels_total": int_total,
-                   "step": ("halo exchange (NCCL all_to_all_single), then the conv of all owned outputs"
+                   "step": ("halo exchange by peer-memory push/wait kernels over NVLink, then the conv of all "
+                            "owned outputs" if peer is not None else
+                            "halo exchange (NCCL all_to_all_single), then the conv of all owned outputs"
                             if reserve < 0 or world == 1 else
                             "halo exchange (NCCL all_to_all_single) beside the conv of interior outputs "
                             f"(on {n_sms - reserve} of {n_sms} SMs), then the conv of boundary outputs") +

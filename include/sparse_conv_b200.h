@@ -208,6 +208,39 @@ SC_API sc_status sc_conv3d_up2(sc_handle* h, const sc_kmap* km, const void* feat
 SC_API sc_status sc_layernorm_silu(sc_handle* h, void* x, int64_t n, int32_t c, sc_dtype dtype, int32_t apply_silu,
                             float eps);
 
+/* ---- Halo exchange over peer memory (sharded convs on the GPUs of one node).
+ * Replaces the NCCL all-to-all of the halo rows (the exchange step of a
+ * Morton-sharded conv); no counterpart in the reference, whose conv runs on
+ * one device.  Every rank allocates a peer buffer, shares its IPC handle
+ * (SC_IPC_HANDLE_BYTES opaque bytes) with the other ranks and opens theirs. */
+#define SC_IPC_HANDLE_BYTES 64
+
+/* Device buffer of `bytes` (zeroed) that other processes can open; the
+ * handle bytes go to `ipc_handle_out`. */
+SC_API sc_status sc_peer_alloc(sc_handle* h, size_t bytes, void** ptr, void* ipc_handle_out);
+SC_API sc_status sc_peer_free(sc_handle* h, void* ptr);
+/* Maps another process's peer buffer into this device's address space. */
+SC_API sc_status sc_peer_open(sc_handle* h, const void* ipc_handle, void** peer_ptr);
+SC_API sc_status sc_peer_close(sc_handle* h, void* peer_ptr);
+
+/* Copies rows to other ranks and signals them: row k of the send list is
+ * `feats` row src_row[k] (row_bytes bytes, a multiple of 16), stored at byte
+ * offset dst_off[k] of peer buffer dst_peer[k] (peer_bufs: device array of
+ * `world` buffer addresses).  When every row has been stored, writes `epoch`
+ * to word `rank` of each peer's flag array (peer_flags: device array of
+ * `world` flag-array addresses).  2 <= world <= 32.  Enqueued on the
+ * handle's stream. */
+SC_API sc_status sc_halo_push(sc_handle* h, const void* feats, int32_t row_bytes, const int32_t* src_row,
+                              const int32_t* dst_peer, const int64_t* dst_off, int64_t n_send,
+                              void* const* peer_bufs, uint32_t* const* peer_flags, int32_t world, int32_t rank,
+                              uint32_t epoch);
+
+/* Waits on the device until word r of `flags` (this rank's flag array) is
+ * >= epoch for every r != rank; a wait longer than one second records
+ * SC_ETIMEOUT in the handle's device error word (see sc_synchronize) and
+ * returns.  Enqueued on the handle's stream. */
+SC_API sc_status sc_halo_wait(sc_handle* h, const uint32_t* flags, int32_t world, int32_t rank, uint32_t epoch);
+
 #ifdef __cplusplus
 }
 #endif

@@ -75,6 +75,16 @@ def _worker(rank, world, port, cfg, scale, ch):
         pkg.conv3d(km_b, buf, W, out=split[ni:])
         torch.cuda.synchronize()
         assert torch.equal(split, out)
+        # halo exchange over peer memory (IPC buffers, push + wait kernels) equals NCCL's
+        px = S.PeerHaloExchange(plan, feats.index_select(0, own), eng)
+        for _ in range(3):  # both regions, twice for the first
+            loc = px.exchange()
+            out_p = pkg.conv3d(km, loc, W)
+            torch.cuda.synchronize()
+            assert torch.equal(loc, loc_f)
+            assert torch.equal(out_p, out)
+        eng.synchronize()  # no device wait timed out
+        px.close()
     finally:
         dist.destroy_process_group()
 

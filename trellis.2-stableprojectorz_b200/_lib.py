@@ -92,7 +92,15 @@ _SIGNATURES = {
     "sc_conv3d_down2": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _U32]),
     "sc_conv3d_up2": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _U32]),
     "sc_layernorm_silu": (_I32, [_P, _P, _I64, _I32, _I32, _I32, _F]),
+    "sc_peer_alloc": (_I32, [_P, ctypes.c_size_t, _PP, _P]),
+    "sc_peer_free": (_I32, [_P, _P]),
+    "sc_peer_open": (_I32, [_P, _P, _PP]),
+    "sc_peer_close": (_I32, [_P, _P]),
+    "sc_halo_push": (_I32, [_P, _P, _I32, _P, _P, _P, _I64, _P, _P, _I32, _I32, _U32]),
+    "sc_halo_wait": (_I32, [_P, _P, _I32, _I32, _U32]),
 }
+
+SC_IPC_HANDLE_BYTES = 64
 
 _lib = None
 _lock = threading.Lock()

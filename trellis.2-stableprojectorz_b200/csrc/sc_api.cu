@@ -147,9 +147,69 @@ sc_status sc_destroy(sc_handle* h) {
     sc::DeviceGuard g(h->impl.device);
     cudaStreamSynchronize(h->impl.stream);
     if (h->impl.derr) cudaFree(h->impl.derr);
+    if (h->impl.push_ticket) cudaFree(h->impl.push_ticket);
   }
   delete h;
   return SC_OK;
+}
+
+sc_status sc_peer_alloc(sc_handle* h, size_t bytes, void** ptr, void* ipc_handle_out) {
+  if (!h || !ptr || !ipc_handle_out) return SC_EINVAL;
+  if (bytes == 0) return sc::set_error(&h->impl, SC_EINVAL, "peer buffer size must be positive");
+  sc::DeviceGuard g(h->impl.device);
+  return sc::peer_alloc(&h->impl, bytes, ptr, ipc_handle_out);
+}
+
+sc_status sc_peer_free(sc_handle* h, void* ptr) {
+  if (!h) return SC_EINVAL;
+  sc::DeviceGuard g(h->impl.device);
+  if (ptr) {
+    const cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess) return sc::cuda_error(&h->impl, e, "free peer buffer");
+  }
+  return SC_OK;
+}
+
+sc_status sc_peer_open(sc_handle* h, const void* ipc_handle, void** peer_ptr) {
+  if (!h || !ipc_handle || !peer_ptr) return SC_EINVAL;
+  sc::DeviceGuard g(h->impl.device);
+  return sc::peer_open(&h->impl, ipc_handle, peer_ptr);
+}
+
+sc_status sc_peer_close(sc_handle* h, void* peer_ptr) {
+  if (!h) return SC_EINVAL;
+  sc::DeviceGuard g(h->impl.device);
+  if (peer_ptr) {
+    const cudaError_t e = cudaIpcCloseMemHandle(peer_ptr);
+    if (e != cudaSuccess) return sc::cuda_error(&h->impl, e, "close peer buffer");
+  }
+  return SC_OK;
+}
+
+sc_status sc_halo_push(sc_handle* h, const void* feats, int32_t row_bytes, const int32_t* src_row,
+                       const int32_t* dst_peer, const int64_t* dst_off, int64_t n_send, void* const* peer_bufs,
+                       uint32_t* const* peer_flags, int32_t world, int32_t rank, uint32_t epoch) {
+  if (!h) return SC_EINVAL;
+  Handle* H = &h->impl;
+  if (world < 2 || world > 32 || rank < 0 || rank >= world)
+    return sc::set_error(H, SC_EINVAL, "halo push: need 2 <= world <= 32 and 0 <= rank < world");
+  if (row_bytes <= 0 || row_bytes % 16 != 0) return sc::set_error(H, SC_EINVAL, "row_bytes must be a multiple of 16");
+  if (n_send < 0) return sc::set_error(H, SC_EINVAL, "n_send must be >= 0");
+  if (!peer_bufs || !peer_flags || (n_send > 0 && (!feats || !src_row || !dst_peer || !dst_off)) ||
+      !sc::aligned(feats, 16))
+    return sc::set_error(H, SC_EINVAL, "halo push: missing or misaligned device arrays");
+  sc::DeviceGuard g(H->device);
+  return sc::halo_push(H, feats, row_bytes, src_row, dst_peer, dst_off, n_send, peer_bufs, peer_flags, world, rank,
+                       epoch);
+}
+
+sc_status sc_halo_wait(sc_handle* h, const uint32_t* flags, int32_t world, int32_t rank, uint32_t epoch) {
+  if (!h) return SC_EINVAL;
+  Handle* H = &h->impl;
+  if (world < 2 || world > 32 || rank < 0 || rank >= world || !flags)
+    return sc::set_error(H, SC_EINVAL, "halo wait: need 2 <= world <= 32, 0 <= rank < world and flags");
+  sc::DeviceGuard g(H->device);
+  return sc::halo_wait(H, flags, world, rank, epoch);
 }
 
 sc_status sc_set_conv_ctas(sc_handle* h, int32_t max_ctas) {

@@ -17,6 +17,7 @@ struct Handle {
   cudaStream_t stream = nullptr;
   int num_sms = 148;
   int conv_ctas = 0;  // CTAs of the tensor-core conv; 0 = one per SM
+  void* push_ticket = nullptr;  // block ticket of the halo push kernel
   int* derr = nullptr;  // device error word written by conv kernels
   unsigned long long launches = 0;  // kernels this handle has launched
   std::string last_error;
@@ -73,6 +74,13 @@ sc_status build_up2(Handle* h, const KMap* down, uint32_t flags, KMap** out);
 sc_status export_map(Handle* h, const KMap* km, int32_t* map_out);
 // allocation-free map build into caller memory (sc_noalloc.cu)
 sc_status ensure_group_order(Handle* h, const KMap* km, int tpi);
+// peer-memory halo exchange
+sc_status peer_alloc(Handle* h, size_t bytes, void** ptr, void* ipc_handle_out);
+sc_status peer_open(Handle* h, const void* ipc_handle, void** peer_ptr);
+sc_status halo_push(Handle* h, const void* feats, int row_bytes, const int32_t* src_row, const int32_t* dst_peer,
+                    const int64_t* dst_off, int64_t n_send, void* const* peer_bufs, uint32_t* const* peer_flags,
+                    int world, int rank, uint32_t epoch);
+sc_status halo_wait(Handle* h, const uint32_t* flags, int world, int rank, uint32_t epoch);
 sc_status build_subm_noalloc(Handle* h, const int32_t* coords, int64_t n, int dilation, int32_t* map_out);
 void free_kmap(Handle* h, KMap* km);
 

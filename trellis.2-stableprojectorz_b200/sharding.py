@@ -32,7 +32,7 @@ import dataclasses
 import torch
 
 __all__ = ["morton_codes", "MortonPartition", "HaloPlan", "build_halo_plan", "exchange_halo", "local_coords",
-           "owned_local"]
+           "owned_local", "PeerHaloExchange"]
 
 _OFFS26 = [(dx, dy, dz) for dx in (-1, 0, 1) for dy in (-1, 0, 1) for dz in (-1, 0, 1) if (dx, dy, dz) != (0, 0, 0)]
 
@@ -160,3 +160,123 @@ def exchange_halo(plan, owned_feats, out=None, group=None, async_op=False):
     work = dist.all_to_all_single(out[plan.n_own:], send, plan.recv_splits, plan.send_splits, group=group,
                                   async_op=async_op)
     return (out, work) if async_op else out
+
+
+class _DeviceArray:
+    """A raw device buffer seen as a torch tensor (``__cuda_array_interface__``)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+_TYPESTR = {torch.bfloat16: "<i2", torch.float16: "<f2", torch.float32: "<f4"}  # bf16 viewed from int16
+
+
+class PeerHaloExchange:
+    """Halo exchange over peer memory: one push kernel and one wait kernel per layer.
+
+    Every rank allocates one peer buffer (``sc_peer_alloc``) holding two local
+    feature regions (owned rows then halo rows, used in alternate exchanges)
+    and one flag word per source rank, and opens the other ranks' buffers by
+    CUDA IPC.  ``exchange()`` stores this rank's send rows straight into the
+    other ranks' halo rows of the next region and waits until every other
+    rank has filled this rank's halo (``sc_halo_push`` / ``sc_halo_wait``, on
+    the current stream).  The caller keeps the owned rows of the region it
+    exchanges in place (``region(parity)[:n_own]``); both regions start with
+    the owned features given to the constructor.  Collective: all ranks build
+    it together and call ``exchange()`` the same number of times.
+    """
+
+    def __init__(self, plan, owned_feats, engine, group=None):
+        import ctypes
+        import torch.distributed as dist
+        from . import _lib as L
+        self.plan, self.engine, self.lib = plan, engine, engine.lib
+        world, rank = plan.world, plan.rank
+        dev = owned_feats.device
+        dtype, channels = owned_feats.dtype, int(owned_feats.shape[1])
+        self.dtype, self.channels = dtype, channels
+        self.row_bytes = channels * owned_feats.element_size()
+        if self.row_bytes % 16:
+            raise ValueError("peer halo exchange needs rows of a multiple of 16 bytes")
+        self.n_rows = plan.n_own + plan.n_halo
+        self.region = (self.n_rows * self.row_bytes + 255) // 256 * 256
+        total = 2 * self.region + 256
+        ptr, handle = ctypes.c_void_p(), (ctypes.c_char * L.SC_IPC_HANDLE_BYTES)()
+        engine.check(self.lib.sc_peer_alloc(engine.handle, total, ctypes.byref(ptr), handle), "sc_peer_alloc")
+        self.base = ptr.value
+        infos = [None] * world
+        dist.all_gather_object(infos, (bytes(handle), plan.n_own, list(plan.recv_splits), self.region), group=group)
+        self.peers = {}
+        for r in range(world):
+            if r == rank:
+                continue
+            pp = ctypes.c_void_p()
+            engine.check(self.lib.sc_peer_open(engine.handle, infos[r][0], ctypes.byref(pp)), "sc_peer_open")
+            self.peers[r] = pp.value
+        bases = [self.base if r == rank else self.peers[r] for r in range(world)]
+        # destination of every send row: peer s, byte offset of row n_own_s + (rows s receives from lower ranks) + j
+        dst_peer, dst_row = [], []
+        for s in range(world):
+            cnt = plan.send_splits[s]
+            if cnt == 0:
+                continue
+            n_own_s, recv_s = infos[s][1], infos[s][2]
+            if recv_s[rank] != cnt:
+                raise RuntimeError(f"halo plan mismatch: rank {s} expects {recv_s[rank]} rows from {rank}, got {cnt}")
+            first = n_own_s + sum(recv_s[:rank])
+            dst_peer += [s] * cnt
+            dst_row += list(range(first, first + cnt))
+        rows = torch.tensor(dst_row, dtype=torch.int64)
+        self.dst_off = [(rows * self.row_bytes + p * torch.tensor([infos[s][3] for s in dst_peer], dtype=torch.int64)
+                         if dst_peer else rows).to(dev) for p in (0, 1)]
+        self.dst_peer = torch.tensor(dst_peer, dtype=torch.int32, device=dev)
+        self.src_row = plan.send_idx.to(device=dev, dtype=torch.int32).contiguous()
+        self.peer_bufs = torch.tensor(bases, dtype=torch.int64, device=dev)
+        self.peer_flags = torch.tensor([b + 2 * infos[r][3] for r, b in enumerate(bases)], dtype=torch.int64,
+                                       device=dev)
+        self.flags = self.base + 2 * self.region
+        self.epoch = 0
+        self.group = group
+        for p in (0, 1):
+            self.region_view(p)[:plan.n_own].copy_(owned_feats)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)
+
+    def region_view(self, parity):
+        """Local features of region `parity`: (n_own + n_halo, C), owned rows first."""
+        arr = _DeviceArray(self.base + parity * self.region, (self.n_rows, self.channels), _TYPESTR[self.dtype])
+        t = torch.as_tensor(arr, device=torch.device("cuda", self.engine.device.index))
+        return t.view(self.dtype) if self.dtype == torch.bfloat16 else t
+
+    def exchange(self):
+        """Fills the halo rows of the next region; returns that region (on the current stream)."""
+        import ctypes
+        self.epoch += 1
+        parity = self.epoch & 1
+        local = self.region_view(parity)
+        eng = self.engine
+        eng.bind_stream()
+        p = self.plan
+        eng.check(self.lib.sc_halo_push(
+            eng.handle, ctypes.c_void_p(local.data_ptr()), self.row_bytes, ctypes.c_void_p(self.src_row.data_ptr()),
+            ctypes.c_void_p(self.dst_peer.data_ptr()), ctypes.c_void_p(self.dst_off[parity].data_ptr()),
+            int(self.src_row.numel()), ctypes.c_void_p(self.peer_bufs.data_ptr()),
+            ctypes.c_void_p(self.peer_flags.data_ptr()), p.world, p.rank, self.epoch), "sc_halo_push")
+        eng.check(self.lib.sc_halo_wait(eng.handle, ctypes.c_void_p(self.flags), p.world, p.rank, self.epoch),
+                  "sc_halo_wait")
+        return local
+
+    def close(self):
+        """Collective: unmaps the peers' buffers and frees this rank's buffer."""
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.engine.device)
+        dist.barrier(group=self.group)
+        for pp in self.peers.values():
+            self.lib.sc_peer_close(self.engine.handle, pp)
+        self.peers = {}
+        dist.barrier(group=self.group)
+        if self.base:
+            self.lib.sc_peer_free(self.engine.handle, self.base)
+            self.base = 0
