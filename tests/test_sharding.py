@@ -109,3 +109,52 @@ def test_partition_is_balanced_and_aligned():
         for r in range(world):
             sib = parent[owner == r]
             assert not torch.isin(sib, parent[owner != r]).any()
+
+
+def _peer_worker(rank, world, port, cfg, scale):
+    import datetime
+    import torch.distributed as dist
+    sys.path.insert(0, ROOT)
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from sparseconv_b200 import sharding as S
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        w = pkg.workloads.make_workload(cfg, scale=scale)
+        coords = torch.from_numpy(w.coords)
+        part = S.MortonPartition.balanced(coords, world)
+        own = part.owned_rows(coords, rank)
+        own_c = coords.index_select(0, own).contiguous()
+        plan = S.build_halo_plan(own_c, part, rank, world)
+        infos = [None] * world
+        dist.all_gather_object(infos, (plan.n_own, list(plan.recv_splits)))
+        dst_peer, dst_row = S.peer_destinations(plan, infos)
+        # what every rank writes where: (dest rank, dest row, coords of the row written)
+        local = S.local_coords(plan, own_c)
+        sent = [(p, r, tuple(local[int(i)].tolist())) for p, r, i in zip(dst_peer, dst_row, plan.send_idx.tolist())]
+        allsent = [None] * world
+        dist.all_gather_object(allsent, sent)
+        # rows written into this rank's buffer tile its halo region exactly, with the plan's halo coords
+        mine = sorted((r, c) for lst in allsent for (p, r, c) in lst if p == rank)
+        assert [r for r, _ in mine] == list(range(plan.n_own, plan.n_own + plan.n_halo))
+        for r, c in mine:
+            assert tuple(local[r].tolist()) == c
+        # a plan that disagrees on the counts is refused
+        if plan.send_splits[(rank + 1) % world] > 0:
+            bad = list(infos)
+            s = (rank + 1) % world
+            bad[s] = (infos[s][0], [x + 1 for x in infos[s][1]])
+            try:
+                S.peer_destinations(plan, bad)
+                raise AssertionError("mismatched plan accepted")
+            except RuntimeError:
+                pass
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_destinations_tile_every_halo(world):
+    mp.spawn(_peer_worker, args=(world, _free_port(), 2, 0.3), nprocs=world, join=True)

@@ -32,7 +32,7 @@ import dataclasses
 import torch
 
 __all__ = ["morton_codes", "MortonPartition", "HaloPlan", "build_halo_plan", "exchange_halo", "local_coords",
-           "owned_local", "PeerHaloExchange"]
+           "owned_local", "peer_destinations", "PeerHaloExchange"]
 
 _OFFS26 = [(dx, dy, dz) for dx in (-1, 0, 1) for dy in (-1, 0, 1) for dz in (-1, 0, 1) if (dx, dy, dz) != (0, 0, 0)]
 
@@ -162,6 +162,29 @@ def exchange_halo(plan, owned_feats, out=None, group=None, async_op=False):
     return (out, work) if async_op else out
 
 
+def peer_destinations(plan, peer_info):
+    """Destination (peer, local row) of each of this rank's send rows, in send order.
+
+    ``peer_info[s] = (n_own_s, recv_splits_s)`` of every rank s.  Rank s keeps
+    its halo rows grouped by source rank after its owned rows, so row j of the
+    rows this rank sends to s lands at ``n_own_s + sum(recv_splits_s[:rank]) + j``.
+    Raises when the plans disagree on the row counts.
+    """
+    dst_peer, dst_row = [], []
+    for s in range(plan.world):
+        cnt = plan.send_splits[s]
+        if cnt == 0:
+            continue
+        n_own_s, recv_s = peer_info[s]
+        if recv_s[plan.rank] != cnt:
+            raise RuntimeError(f"halo plan mismatch: rank {s} expects {recv_s[plan.rank]} rows from "
+                               f"{plan.rank}, got {cnt}")
+        first = n_own_s + sum(recv_s[:plan.rank])
+        dst_peer += [s] * cnt
+        dst_row += list(range(first, first + cnt))
+    return dst_peer, dst_row
+
+
 class _DeviceArray:
     """A raw device buffer seen as a torch tensor (``__cuda_array_interface__``)."""
 
@@ -216,18 +239,7 @@ class PeerHaloExchange:
             engine.check(self.lib.sc_peer_open(engine.handle, infos[r][0], ctypes.byref(pp)), "sc_peer_open")
             self.peers[r] = pp.value
         bases = [self.base if r == rank else self.peers[r] for r in range(world)]
-        # destination of every send row: peer s, byte offset of row n_own_s + (rows s receives from lower ranks) + j
-        dst_peer, dst_row = [], []
-        for s in range(world):
-            cnt = plan.send_splits[s]
-            if cnt == 0:
-                continue
-            n_own_s, recv_s = infos[s][1], infos[s][2]
-            if recv_s[rank] != cnt:
-                raise RuntimeError(f"halo plan mismatch: rank {s} expects {recv_s[rank]} rows from {rank}, got {cnt}")
-            first = n_own_s + sum(recv_s[:rank])
-            dst_peer += [s] * cnt
-            dst_row += list(range(first, first + cnt))
+        dst_peer, dst_row = peer_destinations(plan, [(i[1], i[2]) for i in infos])
         rows = torch.tensor(dst_row, dtype=torch.int64)
         self.dst_off = [(rows * self.row_bytes + p * torch.tensor([infos[s][3] for s in dst_peer], dtype=torch.int64)
                          if dst_peer else rows).to(dev) for p in (0, 1)]
