@@ -205,3 +205,20 @@ def test_large_map_tile_order_matches_unsorted_tiles(pkg, oracle, cuda):
     assert np.array_equal(got[sample], full[sample])
     part = oracle.conv_gather(f.float().cpu().numpy(), full[sample], W.float().cpu().numpy())
     assert rel_l2(out.float().cpu().numpy()[sample], part) < TOL[torch.bfloat16]
+
+
+def test_conv_cta_limit_gives_same_result(pkg, cuda):
+    # fewer persistent CTAs (sc_set_conv_ctas) change the schedule, not the sums
+    w = pkg.workloads.make_workload(2, scale=0.3)
+    c = torch.from_numpy(w.coords).to(cuda)
+    km = pkg.build_kmap(c)
+    f = torch.from_numpy(w.feats).to(cuda, torch.bfloat16)
+    W = torch.from_numpy(w.weight).to(cuda, torch.bfloat16)
+    eng = pkg.get_engine(cuda)
+    ref = pkg.conv3d(km, f, W)
+    try:
+        for ctas in (7, 64):
+            eng.set_conv_ctas(ctas)
+            assert torch.equal(pkg.conv3d(km, f, W), ref)
+    finally:
+        eng.set_conv_ctas(0)

@@ -163,3 +163,16 @@ def test_map_with_fewer_outputs(pkg, oracle, cuda):
             km = pkg.build_kmap(c, n_out=n_out, engine=pkg.get_engine(cuda, mode))
             assert km.n_out == n_out and km.n_in == w.n
             assert np.array_equal(km.export().cpu().numpy(), ref[:n_out]), (n_out, mode)
+
+
+def test_range_build_equals_full_map_rows(pkg, oracle, cuda):
+    # outputs = rows [a, b) (sc_kmap_build_range); neighbours from all rows
+    w = pkg.workloads.make_workload(2, scale=0.25)
+    c = torch.from_numpy(w.coords).to(cuda)
+    full = oracle.kmap_sorted(w.coords, w.spatial_shape)
+    a, b = w.n // 3, w.n // 3 + 777
+    km = pkg.build_kmap(c, out_begin=a, n_out=b - a)
+    assert km.n_out == b - a and km.n_in == w.n
+    assert np.array_equal(km.export().cpu().numpy(), full[a:b])
+    km_tail = pkg.build_kmap(c, out_begin=b)
+    assert np.array_equal(km_tail.export().cpu().numpy(), full[b:])
