@@ -51,9 +51,11 @@ def parse_args():
                     help="c5 on >1 GPU: SMs left to NCCL while the interior conv runs beside the halo exchange; "
                          "-1 (default): exchange first, then one conv over all owned outputs (faster at 2 GPUs, "
                          "where the exchange is 0.04 ms)")
-    ap.add_argument("--c5-exchange", choices=["nccl", "peer"], default="peer",
-                    help="c5 on >1 GPU: halo exchange by the library's peer-memory push/wait kernels over NVLink "
-                         "(default) or by NCCL all_to_all_single")
+    ap.add_argument("--c5-exchange", choices=["nccl", "peer", "peer-conv-wait"], default="peer",
+                    help="c5 on >1 GPU: halo exchange by the library's peer-memory push and wait kernels over NVLink, "
+                         "then the conv (peer, default); the same push, then one conv that runs its interior tiles "
+                         "first and waits for the peers inside its kernel (peer-conv-wait); or NCCL "
+                         "all_to_all_single (nccl)")
     ap.add_argument("--workload", choices=["c2", "c5", "table"], default="c2",
                     help="c2: BASELINE configs[1] (default, data-parallel across ranks); "
                          "c5: configs[4] 1024^3 Morton-sharded across ranks with NCCL halo exchange (strong scaling)")
@@ -401,13 +403,21 @@ def run_c5(args):
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     reserve = args.c5_reserve_sms  # SMs left to the NCCL kernels while the interior conv runs
     peer = None
-    if plan is not None and (reserve < 0 or args.c5_exchange == "peer"):
+    in_kernel_wait = plan is not None and args.c5_exchange == "peer-conv-wait"
+    if in_kernel_wait:
+        kms = [pkg.concat_kmaps(km_i, km_b)]  # interior tiles, then boundary tiles
+    elif plan is not None and (reserve < 0 or args.c5_exchange == "peer"):
         kms = [pkg.build_kmap(loc_c, n_out=n_own, engine=eng)]
-    if plan is not None and args.c5_exchange == "peer":
+    if plan is not None and args.c5_exchange in ("peer", "peer-conv-wait"):
         peer = S.PeerHaloExchange(plan, own_f, eng)
 
     def layer(ev=None):
         """Halo exchange beside the interior conv, then the boundary conv."""
+        if in_kernel_wait:
+            loc, hw = peer.push()
+            if ev: ev[1].record()
+            pkg.conv3d(kms[0], loc, weight, out=out, halo_wait=hw)
+            return
         if peer is not None:
             loc = peer.exchange()
             if ev: ev[1].record()
@@ -478,7 +488,10 @@ def run_c5(args):
         "data": "synthetic: seeded union of 4 ellipsoid shells + 5% interior fill at 1024^3 (BASELINE configs[4])",
         "config": {"workload": w.name, "voxels": w.n, "ci": w.ci, "co": w.co, "pairs": pairs,
                    "halo_voxels_total": halo_total, "interior_voxels_total": int_total,
-                   "step": ("halo exchange by peer-memory push/wait kernels over NVLink, then the conv of all "
+                   "step": ("halo push kernel over NVLink (peer memory), then one conv of all owned outputs that "
+                            "runs its interior tiles first and waits for the peers' pushes inside the kernel before "
+                            "its boundary tiles" if in_kernel_wait else
+                            "halo exchange by peer-memory push/wait kernels over NVLink, then the conv of all "
                             "owned outputs" if peer is not None else
                             "halo exchange (NCCL all_to_all_single), then the conv of all owned outputs"
                             if reserve < 0 or world == 1 else
@@ -487,7 +500,11 @@ def run_c5(args):
                            "; plan and maps built once per coord set",
                    "l2": "flushed between steps by a 256 MB write outside the timed events",
                    "parallelism": f"Morton-range sharding x{world}"},
-        "setup_ms": setup_ms, "exchange_and_interior_ms": 1e3 * t_first / args.steps,
+        "setup_ms": setup_ms,
+        "phases": ("exchange_and_interior_ms = the push kernel, boundary_ms = the conv with its in-kernel wait"
+                   if in_kernel_wait else "exchange_and_interior_ms = exchange (+ interior conv when overlapped), "
+                   "boundary_ms = the conv after it"),
+        "exchange_and_interior_ms": 1e3 * t_first / args.steps,
         "boundary_ms": 1e3 * t_last / args.steps, "ms_per_step_by_rank": [1e3 * t / args.steps for t in per_rank],
         "conv_tflops_total": flops / (t_total / args.steps) / 1e12,
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": float(peaks["hbm_gbs"]) * world,

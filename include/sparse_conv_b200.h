@@ -173,6 +173,16 @@ SC_API sc_status sc_kmap_out_coords(sc_handle* h, const sc_kmap* km, int32_t* co
 SC_API sc_status sc_kmap_build_noalloc(sc_handle* h, const int32_t* coords, int64_t n, int32_t dilation,
                                        int32_t* map_out);
 
+/* Map whose tiles are `first`'s followed by `second`'s: both submanifold maps
+ * over the same input rows, typically two output ranges of one shard built
+ * with sc_kmap_build_range (rows that read no halo row, then the rest).
+ * Output j of `second` becomes output first.n_out + j.  The conv schedules
+ * every tile of `second` after all tiles of `first`, and sc_conv3d_halo waits
+ * for the halo exchange only before those.  Halo data of the parts is not
+ * kept.  No counterpart in the reference (its conv runs on one device). */
+SC_API sc_status sc_kmap_concat(sc_handle* h, const sc_kmap* first, const sc_kmap* second, uint32_t flags,
+                                sc_kmap** out);
+
 /* Writes the canonical int32 [n_out, K] map (for bit-exact checks). */
 SC_API sc_status sc_kmap_export(sc_handle* h, const sc_kmap* km, int32_t* map_out);
 
@@ -234,6 +244,20 @@ SC_API sc_status sc_halo_push(sc_handle* h, const void* feats, int32_t row_bytes
                               const int32_t* dst_peer, const int64_t* dst_off, int64_t n_send,
                               void* const* peer_bufs, uint32_t* const* peer_flags, int32_t world, int32_t rank,
                               uint32_t epoch);
+
+/* sc_conv3d on a submanifold map whose gathers read halo rows filled by
+ * sc_halo_push of exchange `epoch`: the conv waits on the device until word r
+ * of `flags` is >= epoch for every r != rank, inside the conv kernel before
+ * its first tile from the second part of a concatenated map (before its first
+ * tile for other maps), so tiles that read no halo row run while the exchange
+ * is in flight.  The conv finishes only after the exchange has arrived.  A
+ * wait longer than half a second records SC_ETIMEOUT (see sc_synchronize).
+ * f32 convs and the halo-staged kernel wait in a separate launch first.
+ * Replaces sc_halo_wait followed by sc_conv3d. */
+SC_API sc_status sc_conv3d_halo(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight,
+                                const void* bias, const void* residual, void* out, int32_t ci, int32_t co,
+                                sc_dtype dtype, uint32_t epilogue, float ln_eps, const uint32_t* flags,
+                                int32_t world, int32_t rank, uint32_t epoch);
 
 /* Waits on the device until word r of `flags` (this rank's flag array) is
  * >= epoch for every r != rank; a wait longer than one second records

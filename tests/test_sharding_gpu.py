@@ -83,6 +83,22 @@ def _worker(rank, world, port, cfg, scale, ch):
             torch.cuda.synchronize()
             assert torch.equal(loc, loc_f)
             assert torch.equal(out_p, out)
+        # push only; the conv on the interior+boundary map waits in its kernel
+        km_c = pkg.concat_kmaps(km_i, km_b)
+        for _ in range(4):
+            loc, hw = px.push()
+            out_c = pkg.conv3d(km_c, loc, W, halo_wait=hw)
+            torch.cuda.synchronize()
+            assert torch.equal(loc, loc_f)
+            assert torch.equal(out_c, out)
+        # back-to-back layers without host synchronisation
+        outs = []
+        for _ in range(6):
+            loc, hw = px.push()
+            outs.append(pkg.conv3d(km_c, loc, W, halo_wait=hw))
+        torch.cuda.synchronize()
+        for o in outs:
+            assert torch.equal(o, out)
         eng.synchronize()  # no device wait timed out
         px.close()
     finally:

@@ -11,7 +11,7 @@ host-to-host pipeline that overlaps the transfers of consecutive calls.  All com
 from . import _lib
 from ._lib import SparseConvError, DuplicateCoordError, CoordRangeError
 from .sparse_conv import (
-    Engine, get_engine, KernelMap, build_kmap, build_down2, build_up2, conv3d, layernorm_silu,
+    Engine, get_engine, KernelMap, build_kmap, concat_kmaps, HaloWait, build_down2, build_up2, conv3d, layernorm_silu,
     SparseTensor, SparseConv3d, SparseConvDown2, SparseConvUp2, sparse_conv3d_forward, sparse_resblock,
 )
 from .host_pipeline import HostConvPipeline

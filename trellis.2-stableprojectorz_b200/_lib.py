@@ -84,6 +84,7 @@ _SIGNATURES = {
     "sc_kmap_build_noalloc": (_I32, [_P, _P, _I64, _I32, _P]),
     "sc_kmap_out_coords": (_I32, [_P, _P, _P]),
     "sc_kmap_export": (_I32, [_P, _P, _P]),
+    "sc_kmap_concat": (_I32, [_P, _P, _P, _U32, _PP]),
     "sc_kmap_get_info": (_I32, [_P, _P, ctypes.POINTER(ScKmapInfo)]),
     "sc_kmap_check": (_I32, [_P, _P]),
     "sc_kmap_free": (_I32, [_P, _P]),
@@ -98,6 +99,7 @@ _SIGNATURES = {
     "sc_peer_close": (_I32, [_P, _P]),
     "sc_halo_push": (_I32, [_P, _P, _I32, _P, _P, _P, _I64, _P, _P, _I32, _I32, _U32]),
     "sc_halo_wait": (_I32, [_P, _P, _I32, _I32, _U32]),
+    "sc_conv3d_halo": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _U32, _F, _P, _I32, _I32, _U32]),
 }
 
 SC_IPC_HANDLE_BYTES = 64

@@ -291,6 +291,17 @@ sc_status sc_kmap_build_ex(sc_handle* h, const int32_t* coords, int64_t n_in, in
   return sc_kmap_build_range(h, coords, n_in, 0, n_out, kernel_size, dilation, flags, out);
 }
 
+sc_status sc_kmap_concat(sc_handle* h, const sc_kmap* first, const sc_kmap* second, uint32_t flags, sc_kmap** out) {
+  if (!h || !out || !first || !second) return SC_EINVAL;
+  *out = nullptr;
+  Handle* H = &h->impl;
+  sc::DeviceGuard g(H->device);
+  KMap* km = nullptr;
+  const sc_status st = sc::concat_maps(H, first->impl, second->impl, &km);
+  if (st != SC_OK) return st;
+  return wrap_kmap(H, km, flags, out);
+}
+
 sc_status sc_kmap_build_down2(sc_handle* h, const int32_t* coords, int64_t n, uint32_t flags, sc_kmap** out) {
   if (!h || !out) return SC_EINVAL;
   *out = nullptr;
@@ -382,29 +393,56 @@ sc_status sc_kmap_free(sc_handle* h, sc_kmap* km) {
   return SC_OK;
 }
 
-sc_status sc_conv3d(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight, const void* bias,
-                    const void* residual, void* out, int32_t ci, int32_t co, sc_dtype dtype, uint32_t epilogue,
-                    float ln_eps) {
+namespace {
+
+sc_status conv3d_impl(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight, const void* bias,
+                      const void* residual, void* out, int32_t ci, int32_t co, sc_dtype dtype, uint32_t epilogue,
+                      float ln_eps, const sc::ConvWait& wait) {
   if (!h || !km) return SC_EINVAL;
   Handle* H = &h->impl;
   const KMap* K = km->impl;
   if (ci <= 0 || co <= 0) return sc::set_error(H, SC_EINVAL, "channel counts must be positive");
   if (epilogue & ~(SC_EPI_SILU | SC_EPI_RESIDUAL | SC_EPI_LAYERNORM))
     return sc::set_error(H, SC_EINVAL, "unknown epilogue flag");
-  if (K->n_out == 0) return SC_OK;
+  if (dtype != SC_F32 && dtype != SC_BF16 && dtype != SC_F16) return sc::set_error(H, SC_EINVAL, "unknown dtype");
+  sc::DeviceGuard g(H->device);
+  if (K->n_out == 0) return wait.flags ? sc::halo_wait(H, wait.flags, wait.world, wait.rank, wait.epoch) : SC_OK;
   if (!weight || !out || (K->n_in > 0 && !feats)) return sc::set_error(H, SC_EINVAL, "null operand");
   if ((epilogue & SC_EPI_RESIDUAL) && !residual) return sc::set_error(H, SC_EINVAL, "residual missing");
   if (!(ln_eps >= 0.f)) return sc::set_error(H, SC_EINVAL, "ln_eps must be >= 0");
-  sc::DeviceGuard g(H->device);
   if (dtype == SC_F32) {
+    if (wait.flags) {
+      const sc_status st = sc::halo_wait(H, wait.flags, wait.world, wait.rank, wait.epoch);
+      if (st != SC_OK) return st;
+    }
     return sc::conv_simt_f32(H, K, static_cast<const float*>(feats), static_cast<const float*>(weight),
                              static_cast<const float*>(bias), static_cast<const float*>(residual),
                              static_cast<float*>(out), ci, co, epilogue, ln_eps);
   }
-  if (dtype == SC_BF16 || dtype == SC_F16) {
-    return sc::conv_tc(H, K, feats, weight, bias, residual, out, ci, co, dtype, epilogue, ln_eps);
-  }
-  return sc::set_error(H, SC_EINVAL, "unknown dtype");
+  return sc::conv_tc(H, K, feats, weight, bias, residual, out, ci, co, dtype, epilogue, ln_eps, wait);
+}
+
+}  // namespace
+
+sc_status sc_conv3d(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight, const void* bias,
+                    const void* residual, void* out, int32_t ci, int32_t co, sc_dtype dtype, uint32_t epilogue,
+                    float ln_eps) {
+  return conv3d_impl(h, km, feats, weight, bias, residual, out, ci, co, dtype, epilogue, ln_eps, sc::ConvWait());
+}
+
+sc_status sc_conv3d_halo(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight, const void* bias,
+                         const void* residual, void* out, int32_t ci, int32_t co, sc_dtype dtype, uint32_t epilogue,
+                         float ln_eps, const uint32_t* flags, int32_t world, int32_t rank, uint32_t epoch) {
+  if (!h || !km) return SC_EINVAL;
+  if (world < 2 || world > 32 || rank < 0 || rank >= world || !flags)
+    return sc::set_error(&h->impl, SC_EINVAL, "conv halo wait: need 2 <= world <= 32, 0 <= rank < world and flags");
+  if (km->impl->kind != SC_KMAP_SUBM) return sc::set_error(&h->impl, SC_EINVAL, "map is not a submanifold map");
+  sc::ConvWait w;
+  w.flags = flags;
+  w.world = world;
+  w.rank = rank;
+  w.epoch = epoch;
+  return conv3d_impl(h, km, feats, weight, bias, residual, out, ci, co, dtype, epilogue, ln_eps, w);
 }
 
 sc_status sc_conv3d_subm(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight, const void* bias,

@@ -65,7 +65,43 @@ struct TcParams {
   uint32_t epi;
   float eps;
   int* err;
+  // Halo exchange to wait for (null flags: none).  Groups ending past
+  // wait_tile gather halo rows: a producer warp waits for the exchange before
+  // its first such group, and at the latest before it exits.
+  const uint32_t* wait_flags;
+  int64_t wait_tile;
+  uint32_t wait_epoch;
+  int wait_world;
+  int wait_rank;
 };
+
+// Warp-wide bounded wait for a halo exchange: lane r polls word r of `flags`
+// (r < world, r != rank) with system-scope acquire loads until it reaches
+// `epoch` (wrap-safe), then the warp synchronises, so every lane's later loads
+// see the rows the peers stored before publishing.  Gives up after half the
+// pipeline wait limit with SC_ETIMEOUT, so a late exchange never lets the
+// conv's own stage waits (started no earlier) run out first.
+constexpr unsigned long long kHaloFlagLimitNs = kWaitLimitNs / 2;
+__device__ __forceinline__ void halo_flags_wait_warp(const uint32_t* flags, int world, int rank, uint32_t epoch,
+                                                     int* err) {
+  const int r = threadIdx.x & 31;
+  if (r < world && r != rank) {
+    const unsigned long long t0 = globaltimer_ns();
+    unsigned ns = 32;
+    for (;;) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+      if (static_cast<int32_t>(v - epoch) >= 0) break;
+      if (globaltimer_ns() - t0 > kHaloFlagLimitNs) {
+        record_error(err, SC_ETIMEOUT);
+        break;
+      }
+      __nanosleep(ns);
+      if (ns < 256) ns <<= 1;
+    }
+  }
+  __syncwarp();
+}
 
 constexpr int kProducers = 128;  // warps 0-3
 constexpr int kMmaWarp = 4;
@@ -305,6 +341,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // a shared load issued after this thread's cp.async waits for those
     // copies to land and would serialise the pipeline.
     bool abort = false;
+    bool waited = p.wait_flags == nullptr;
     // gather-index prefetch: warp w loads active offsets j = w, w+4, ... (<= 7 each)
     int4 pre[7][TPI];
     auto load_idx = [&](int64_t item) {
@@ -345,6 +382,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       named_bar_sync(1, kProducers);  // idx_s holds this group's indices
       int cb;
       const int64_t g = item_group(item, cb);
+      if (!waited && min((g + 1) * TPI, p.num_tiles) > p.wait_tile) {
+        halo_flags_wait_warp(p.wait_flags, p.wait_world, p.wait_rank, p.wait_epoch, p.err);
+        waited = true;
+      }
       int64_t round_next = round + 1;
       const int64_t next = next_item(round_next);
       const int nact_next = next >= 0 ? load_idx(next) : 0;
@@ -407,6 +448,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       round = round_next;
       item = next;
     }
+    // The kernel ends only after the exchange has arrived, also when this
+    // CTA gathered no halo row: the caller's next exchange may then reuse
+    // the peers' buffers.
+    if (!waited) halo_flags_wait_warp(p.wait_flags, p.wait_world, p.wait_rank, p.wait_epoch, p.err);
     cp_async_wait_all();
     if (abort && pt == 0) {
       // Error exit: let weight copies already issued into our shared memory land.
@@ -1077,7 +1122,8 @@ bool halo_applies(const Handle* h, const KMap* km, int ci, int co) {
 }
 
 sc_status conv_tc(Handle* h, const KMap* km, const void* feats, const void* weight, const void* bias,
-                  const void* residual, void* out, int ci, int co, sc_dtype dtype, uint32_t epi, float eps) {
+                  const void* residual, void* out, int ci, int co, sc_dtype dtype, uint32_t epi, float eps,
+                  const ConvWait& wait) {
   if (ci % 16 != 0 || co % 16 != 0)
     return set_error(h, SC_EUNSUPPORTED, "bf16/f16 conv needs Ci and Co multiples of 16");
   if (km->n_in <= 0) return set_error(h, SC_EINVAL, "map has no input rows");
@@ -1098,9 +1144,15 @@ sc_status conv_tc(Handle* h, const KMap* km, const void* feats, const void* weig
     const sc_status st = check_gather_bounds(h, km);
     if (st != SC_OK) return st;
   }
-  if (halo_applies(h, km, ci, co))
+  if (halo_applies(h, km, ci, co)) {
+    // the halo-staged kernel takes the exchange's wait as a separate launch
+    if (wait.flags) {
+      const sc_status st = halo_wait(h, wait.flags, wait.world, wait.rank, wait.epoch);
+      if (st != SC_OK) return st;
+    }
     return dtype == SC_BF16 ? launch_halo<true>(h, km, feats, weight, bias, residual, out, ci, co, epi, eps)
                             : launch_halo<false>(h, km, feats, weight, bias, residual, out, ci, co, epi, eps);
+  }
   TcParams p{};
   p.gidx = km->gidx;
   p.tile_rows = km->tile_rows;
@@ -1118,7 +1170,14 @@ sc_status conv_tc(Handle* h, const KMap* km, const void* feats, const void* weig
   p.epi = epi;
   p.eps = eps;
   p.err = h->derr;
-  if (p.num_items == 0) return SC_OK;
+  if (p.num_items == 0) return wait.flags ? halo_wait(h, wait.flags, wait.world, wait.rank, wait.epoch) : SC_OK;
+  // A plain map may read halo rows from its first tile; a concatenated map
+  // from its second part on.
+  p.wait_flags = wait.flags;
+  p.wait_tile = km->split_tile >= 0 ? km->split_tile : 0;
+  p.wait_epoch = wait.epoch;
+  p.wait_world = wait.world;
+  p.wait_rank = wait.rank;
   return dtype == SC_BF16 ? dispatch_kc<true>(h, km, feats, weight, p)
                           : dispatch_kc<false>(h, km, feats, weight, p);
 }

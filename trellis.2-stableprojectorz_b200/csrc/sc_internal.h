@@ -56,6 +56,9 @@ struct KMap {
   int32_t* halo_rows = nullptr;   // [num_tiles][kHaloCap]
   int32_t* halo_n = nullptr;      // [num_tiles]
   uint16_t* lidx = nullptr;       // [num_tiles][27][128]
+  // Concatenated maps (concat_maps): tiles [split_tile, num_tiles) came from
+  // the second map and are scheduled after every earlier tile; -1 = no split.
+  int64_t split_tile = -1;
   int32_t* out_coords = nullptr;   // down-sample: parent coords [n_out, 4]
   int32_t* parent_of = nullptr;    // down-sample: parent of every fine row [n_in]
   unsigned long long* counters = nullptr;  // [0] valid pairs, [1] tile pairs
@@ -81,12 +84,23 @@ sc_status halo_push(Handle* h, const void* feats, int row_bytes, const int32_t* 
                     const int64_t* dst_off, int64_t n_send, void* const* peer_bufs, uint32_t* const* peer_flags,
                     int world, int rank, uint32_t epoch);
 sc_status halo_wait(Handle* h, const uint32_t* flags, int world, int rank, uint32_t epoch);
+sc_status concat_maps(Handle* h, const KMap* a, const KMap* b, KMap** out);
 sc_status build_subm_noalloc(Handle* h, const int32_t* coords, int64_t n, int dilation, int32_t* map_out);
 void free_kmap(Handle* h, KMap* km);
 
+// A halo exchange the conv waits for on the device before it gathers halo
+// rows: word r of `flags` must reach `epoch` for every r != rank.
+struct ConvWait {
+  const uint32_t* flags = nullptr;
+  int world = 0;
+  int rank = 0;
+  uint32_t epoch = 0;
+};
+
 // conv launchers
 sc_status conv_tc(Handle* h, const KMap* km, const void* feats, const void* weight, const void* bias,
-                  const void* residual, void* out, int ci, int co, sc_dtype dtype, uint32_t epi, float eps);
+                  const void* residual, void* out, int ci, int co, sc_dtype dtype, uint32_t epi, float eps,
+                  const ConvWait& wait = ConvWait());
 sc_status conv_simt_f32(Handle* h, const KMap* km, const float* feats, const float* weight, const float* bias,
                         const float* residual, float* out, int ci, int co, uint32_t epi, float eps);
 sc_status check_gather_bounds(Handle* h, const KMap* km);

@@ -87,6 +87,30 @@ __device__ __forceinline__ void offset27(int v, int dil, int& dx, int& dy, int& 
   dz = (v % 3 - 1) * dil;
 }
 
+// Tile rows of a concatenated map: the first map's slots, then the second
+// map's with every output row shifted by the first map's output count.
+__global__ void k_concat_rows(const int32_t* __restrict__ a_rows, int64_t a_slots, const int32_t* __restrict__ b_rows,
+                              int64_t b_slots, int32_t shift, int32_t* __restrict__ rows) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i < a_slots) {
+    rows[i] = a_rows[i];
+  } else if (i < a_slots + b_slots) {
+    const int32_t r = b_rows[i - a_slots];
+    rows[i] = r >= 0 ? r + shift : -1;
+  }
+}
+
+// Pair counters of a concatenated map are the sums of its parts'; the build
+// status is the first part's error, else the second's.
+__global__ void k_concat_counters(const unsigned long long* a, const int* a_err, const unsigned long long* b,
+                                  const int* b_err, unsigned long long* c, int* c_err) {
+  if (threadIdx.x == 0) {
+    c[0] = a[0] + b[0];
+    c[1] = a[1] + b[1];
+    *c_err = *a_err ? *a_err : *b_err;
+  }
+}
+
 __global__ void k_iota(uint32_t* v, int64_t n) {
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (i < n) v[i] = static_cast<uint32_t>(i);
@@ -544,30 +568,34 @@ __global__ void k_sort_keys(const uint32_t* __restrict__ row_mask, int64_t n, in
 // a counting sort in two passes (bucket sizes, then placement).  The order
 // within a bucket depends on atomic timing; conv results do not, since every
 // output row sums its offsets in the same order whichever CTA computes it.
-constexpr int kWorkBuckets = 33;  // offsets per group: 0..32
+// Groups holding a tile at or past `split` (the second part of a concatenated
+// map) form a second class of buckets placed after the first.
+constexpr int kWorkBuckets = 66;  // (late class) x (offsets per group: 0..32)
 
-__device__ __forceinline__ int group_bucket(const uint32_t* tile_mask, int64_t g, int64_t num_tiles, int tpi) {
+__device__ __forceinline__ int group_bucket(const uint32_t* tile_mask, int64_t g, int64_t num_tiles, int tpi,
+                                            int64_t split) {
   uint32_t m = 0;
   for (int i = 0; i < tpi; ++i)
     if (g * tpi + i < num_tiles) m |= tile_mask[g * tpi + i];
-  return 32 - __popc(m);  // more offsets first
+  const int64_t end = (g + 1) * tpi < num_tiles ? (g + 1) * tpi : num_tiles;
+  return 32 - __popc(m) + (end > split ? 33 : 0);  // more offsets first, late class last
 }
 
 __global__ void k_group_hist(const uint32_t* __restrict__ tile_mask, int64_t num_tiles, int tpi, int64_t groups,
-                             uint32_t* hist) {
+                             int64_t split, uint32_t* hist) {
   __shared__ uint32_t sh[kWorkBuckets];
   for (int b = threadIdx.x; b < kWorkBuckets; b += blockDim.x) sh[b] = 0;
   __syncthreads();
   for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
        g += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    atomicAdd(&sh[group_bucket(tile_mask, g, num_tiles, tpi)], 1u);
+    atomicAdd(&sh[group_bucket(tile_mask, g, num_tiles, tpi, split)], 1u);
   __syncthreads();
   for (int b = threadIdx.x; b < kWorkBuckets; b += blockDim.x)
     if (sh[b]) atomicAdd(&hist[b], sh[b]);
 }
 
 __global__ void k_group_place(const uint32_t* __restrict__ tile_mask, int64_t num_tiles, int tpi, int64_t groups,
-                              const uint32_t* __restrict__ hist, uint32_t* cursor, int32_t* order) {
+                              int64_t split, const uint32_t* __restrict__ hist, uint32_t* cursor, int32_t* order) {
   __shared__ uint32_t base[kWorkBuckets];
   if (threadIdx.x == 0) {
     uint32_t acc = 0;
@@ -579,7 +607,7 @@ __global__ void k_group_place(const uint32_t* __restrict__ tile_mask, int64_t nu
   __syncthreads();
   for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
        g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int b = group_bucket(tile_mask, g, num_tiles, tpi);
+    const int b = group_bucket(tile_mask, g, num_tiles, tpi, split);
     order[base[b] + atomicAdd(&cursor[b], 1u)] = static_cast<int32_t>(g);
   }
 }
@@ -777,10 +805,11 @@ sc_status ensure_group_order(Handle* h, const KMap* km, int tpi) {
     SC_TRY_CUDA(tmp.get(&counts, sizeof(uint32_t) * 2 * kWorkBuckets), "alloc group counts");
     SC_TRY_CUDA(cudaMemsetAsync(counts, 0, sizeof(uint32_t) * 2 * kWorkBuckets, h->stream), "clear group counts");
     const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((groups + 255) / 256, 4 * h->num_sms));
+    const int64_t split = km->split_tile >= 0 ? km->split_tile : km->num_tiles;
     ++h->launches;
-    k_group_hist<<<blocks, 256, 0, h->stream>>>(km->tile_mask, km->num_tiles, tpi, groups, counts);
+    k_group_hist<<<blocks, 256, 0, h->stream>>>(km->tile_mask, km->num_tiles, tpi, groups, split, counts);
     ++h->launches;
-    k_group_place<<<blocks, 256, 0, h->stream>>>(km->tile_mask, km->num_tiles, tpi, groups, counts,
+    k_group_place<<<blocks, 256, 0, h->stream>>>(km->tile_mask, km->num_tiles, tpi, groups, split, counts,
                                                  counts + kWorkBuckets, km->group_order[t]);
     SC_TRY_CUDA(cudaGetLastError(), "group order launch");
   }
@@ -1043,6 +1072,51 @@ void free_kmap(Handle* h, KMap* km) {
   dev_free(h, km->parent_of);
   dev_free(h, km->counters);
   delete km;
+}
+
+sc_status concat_maps(Handle* h, const KMap* a, const KMap* b, KMap** out) {
+  if (a->kind != SC_KMAP_SUBM || b->kind != SC_KMAP_SUBM || a->K != b->K || a->n_in != b->n_in)
+    return set_error(h, SC_EINVAL, "concat: both maps must be submanifold maps over the same input rows");
+  if (a->n_out + b->n_out >= (1ll << 31)) return set_error(h, SC_EINVAL, "concat: too many output rows");
+  KMap* km = nullptr;
+  sc_status st = new_kmap(h, SC_KMAP_SUBM, a->K, a->n_in, a->n_out + b->n_out, &km);
+  if (st != SC_OK) return st;
+  km->num_tiles = a->num_tiles + b->num_tiles;
+  km->split_tile = a->num_tiles;
+  const int64_t T = km->num_tiles, slots = std::max<int64_t>(T, 1) * kTileRows;
+  cudaError_t e = dev_alloc(h, reinterpret_cast<void**>(&km->gidx), sizeof(int32_t) * slots * km->K);
+  if (e == cudaSuccess) e = dev_alloc(h, reinterpret_cast<void**>(&km->tile_rows), sizeof(int32_t) * slots);
+  if (e == cudaSuccess)
+    e = dev_alloc(h, reinterpret_cast<void**>(&km->tile_mask), sizeof(uint32_t) * std::max<int64_t>(T, 1));
+  const size_t ga = sizeof(int32_t) * a->num_tiles * a->K * kTileRows;
+  const size_t gb = sizeof(int32_t) * b->num_tiles * b->K * kTileRows;
+  if (e == cudaSuccess && ga) e = cudaMemcpyAsync(km->gidx, a->gidx, ga, cudaMemcpyDeviceToDevice, h->stream);
+  if (e == cudaSuccess && gb)
+    e = cudaMemcpyAsync(reinterpret_cast<uint8_t*>(km->gidx) + ga, b->gidx, gb, cudaMemcpyDeviceToDevice, h->stream);
+  if (e == cudaSuccess && a->num_tiles)
+    e = cudaMemcpyAsync(km->tile_mask, a->tile_mask, sizeof(uint32_t) * a->num_tiles, cudaMemcpyDeviceToDevice,
+                        h->stream);
+  if (e == cudaSuccess && b->num_tiles)
+    e = cudaMemcpyAsync(km->tile_mask + a->num_tiles, b->tile_mask, sizeof(uint32_t) * b->num_tiles,
+                        cudaMemcpyDeviceToDevice, h->stream);
+  if (e == cudaSuccess && T) {
+    ++h->launches;
+    k_concat_rows<<<blocks_for(T * kTileRows, 256), 256, 0, h->stream>>>(
+        a->tile_rows, a->num_tiles * kTileRows, b->tile_rows, b->num_tiles * kTileRows, static_cast<int32_t>(a->n_out),
+        km->tile_rows);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) {
+    ++h->launches;
+    k_concat_counters<<<1, 32, 0, h->stream>>>(a->counters, a->err, b->counters, b->err, km->counters, km->err);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    free_kmap(h, km);
+    return cuda_error(h, e, "concat maps");
+  }
+  *out = km;
+  return SC_OK;
 }
 
 }  // namespace sc

@@ -38,12 +38,16 @@ __global__ void __launch_bounds__(kPushThreads) k_halo_push(const uint4* __restr
     const uint4 val = __ldg(feats + static_cast<int64_t>(src_row[k]) * row_vecs + c);
     reinterpret_cast<uint4*>(static_cast<uint8_t*>(peer_bufs[dst_peer[k]]) + dst_off[k])[c] = val;
   }
-  // Every thread orders its row stores before the block's ticket; the last
-  // block to take a ticket publishes the epoch to every peer.
-  __threadfence_system();
+  // The block barrier orders every thread's row stores before thread 0's
+  // system-scope fence (fences are cumulative over what the barrier made
+  // visible to thread 0), which orders them before the block's ticket; the
+  // last block to take a ticket publishes the epoch to every peer.  One fence
+  // per block rather than one per thread: each system-scope fence waits for
+  // the stores it orders to be acknowledged.
   __syncthreads();
   __shared__ bool last;
   if (threadIdx.x == 0) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
     unsigned int prev;
     asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ticket) : "memory");
     last = prev == gridDim.x - 1;

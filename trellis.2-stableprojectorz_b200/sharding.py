@@ -197,7 +197,7 @@ _TYPESTR = {torch.bfloat16: "<i2", torch.float16: "<f2", torch.float32: "<f4"}  
 
 
 class PeerHaloExchange:
-    """Halo exchange over peer memory: one push kernel and one wait kernel per layer.
+    """Halo exchange over peer memory: one push kernel per layer, waited for by a wait kernel or by the conv.
 
     Every rank allocates one peer buffer (``sc_peer_alloc``) holding two local
     feature regions (owned rows then halo rows, used in alternate exchanges)
@@ -205,10 +205,14 @@ class PeerHaloExchange:
     CUDA IPC.  ``exchange()`` stores this rank's send rows straight into the
     other ranks' halo rows of the next region and waits until every other
     rank has filled this rank's halo (``sc_halo_push`` / ``sc_halo_wait``, on
-    the current stream).  The caller keeps the owned rows of the region it
-    exchanges in place (``region(parity)[:n_own]``); both regions start with
-    the owned features given to the constructor.  Collective: all ranks build
-    it together and call ``exchange()`` the same number of times.
+    the current stream).  ``push()`` only stores and signals; the conv that
+    follows waits inside its kernel, before its first tile that reads a halo
+    row (``conv3d(..., halo_wait=...)`` on a map from ``concat_kmaps`` of the
+    interior and boundary outputs), so the interior tiles hide the exchange.
+    The caller keeps the owned rows of the region it exchanges in place
+    (``region(parity)[:n_own]``); both regions start with the owned features
+    given to the constructor.  Collective: all ranks build it together and
+    call ``exchange()`` / ``push()`` the same number of times.
     """
 
     def __init__(self, plan, owned_feats, engine, group=None):
@@ -265,20 +269,41 @@ class PeerHaloExchange:
     def exchange(self):
         """Fills the halo rows of the next region; returns that region (on the current stream)."""
         import ctypes
+        local, hw = self.push()
+        eng = self.engine
+        eng.check(self.lib.sc_halo_wait(eng.handle, ctypes.c_void_p(hw.flags), hw.world, hw.rank, hw.epoch),
+                  "sc_halo_wait")
+        return local
+
+    def push(self):
+        """Starts the next exchange without waiting for it, on the current
+        stream: returns the region and a :class:`HaloWait` for
+        ``conv3d(..., halo_wait=...)``, which waits on the device before
+        gathering halo rows.  Pair every ``push()`` with one such conv (or
+        ``sc_halo_wait``) before the next ``push()``: that wait keeps this rank
+        at most one exchange ahead of its peers.
+
+        The push kernel must complete before the conv that waits for the
+        peers' pushes starts (stream order): a push enqueued beside that conv
+        (another stream) may find no free SM while the conv's CTAs wait for a
+        peer whose own conv waits for this push, and the waits then run out."""
+        from .sparse_conv import HaloWait
         self.epoch += 1
         parity = self.epoch & 1
         local = self.region_view(parity)
-        eng = self.engine
-        eng.bind_stream()
+        self._enqueue_push(local, parity)
         p = self.plan
+        return local, HaloWait(self.flags, p.world, p.rank, self.epoch)
+
+    def _enqueue_push(self, local, parity):
+        import ctypes
+        eng, p = self.engine, self.plan
+        eng.bind_stream()
         eng.check(self.lib.sc_halo_push(
             eng.handle, ctypes.c_void_p(local.data_ptr()), self.row_bytes, ctypes.c_void_p(self.src_row.data_ptr()),
             ctypes.c_void_p(self.dst_peer.data_ptr()), ctypes.c_void_p(self.dst_off[parity].data_ptr()),
             int(self.src_row.numel()), ctypes.c_void_p(self.peer_bufs.data_ptr()),
             ctypes.c_void_p(self.peer_flags.data_ptr()), p.world, p.rank, self.epoch), "sc_halo_push")
-        eng.check(self.lib.sc_halo_wait(eng.handle, ctypes.c_void_p(self.flags), p.world, p.rank, self.epoch),
-                  "sc_halo_wait")
-        return local
 
     def close(self):
         """Collective: unmaps the peers' buffers and frees this rank's buffer."""

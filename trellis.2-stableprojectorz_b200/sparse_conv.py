@@ -18,6 +18,7 @@ library surface as ``SparseConvError`` (``DuplicateCoordError`` /
 """
 from __future__ import annotations
 
+import collections
 import ctypes
 import threading
 
@@ -196,6 +197,32 @@ def build_kmap(coords, dilation=1, engine=None, tile_sort=True, check=True, n_ou
     return KernelMap(eng, p, L.SC_KMAP_SUBM, n, n_out, 27)
 
 
+def concat_kmaps(first, second, check=True):
+    """Map whose tiles are ``first``'s then ``second``'s (``sc_kmap_concat``).
+
+    Both are submanifold maps over the same input rows; output j of ``second``
+    becomes output ``first.n_out + j``.  A sharded conv concatenates the map of
+    its interior outputs (which read no halo row) with that of its boundary
+    outputs, so ``conv3d(..., halo_wait=...)`` runs the interior tiles while
+    the halo exchange is in flight.
+    """
+    if first.kind != L.SC_KMAP_SUBM or second.kind != L.SC_KMAP_SUBM:
+        raise ValueError("concat_kmaps needs two submanifold maps")
+    if first.engine is not second.engine or first.n_in != second.n_in:
+        raise ValueError("concat_kmaps needs maps of one engine over the same input rows")
+    eng = first.engine
+    eng.bind_stream()
+    p = ctypes.c_void_p()
+    eng.check(eng.lib.sc_kmap_concat(eng.handle, first.ptr, second.ptr, _flags(True, check),
+                                     ctypes.byref(p)), "sc_kmap_concat")
+    return KernelMap(eng, p, L.SC_KMAP_SUBM, first.n_in, first.n_out + second.n_out, first.kernel_volume)
+
+
+class HaloWait(collections.namedtuple("HaloWait", "flags world rank epoch")):
+    """A halo exchange a conv waits for on the device: word r of the flag array
+    at device address ``flags`` must reach ``epoch`` for every r != rank."""
+
+
 def build_down2(coords, engine=None, tile_sort=True):
     """Stride-2 2x2x2 down-sample map (``sc_kmap_build_down2``)."""
     coords = _coords_arg(coords)
@@ -217,8 +244,13 @@ def build_up2(down, tile_sort=True):
     return KernelMap(eng, p, L.SC_KMAP_UP2, down.n_out, down.n_in, 8, keepalive=down)
 
 
-def conv3d(kmap, feats, weight, bias=None, residual=None, silu=False, layernorm=False, eps=1e-6, out=None):
-    """``out = epilogue(bias + sum_v W[:, v] . feats[map[:, v]])`` through ``sc_conv3d``."""
+def conv3d(kmap, feats, weight, bias=None, residual=None, silu=False, layernorm=False, eps=1e-6, out=None,
+           halo_wait=None):
+    """``out = epilogue(bias + sum_v W[:, v] . feats[map[:, v]])`` through ``sc_conv3d``.
+
+    With ``halo_wait`` (a :class:`HaloWait`) the conv waits on the device for
+    that halo exchange before it gathers halo rows (``sc_conv3d_halo``).
+    """
     dt = _DTYPES.get(feats.dtype)
     if dt is None:
         raise TypeError(f"unsupported feature dtype {feats.dtype}")
@@ -241,8 +273,15 @@ def conv3d(kmap, feats, weight, bias=None, residual=None, silu=False, layernorm=
           (L.SC_EPI_LAYERNORM if layernorm else 0)
     eng = kmap.engine
     eng.bind_stream()
-    eng.check(eng.lib.sc_conv3d(eng.handle, kmap.ptr, _ptr(feats), _ptr(weight), _ptr(bias), _ptr(residual),
-                                _ptr(out), ci, co, dt, epi, float(eps)), "sc_conv3d")
+    if halo_wait is None:
+        eng.check(eng.lib.sc_conv3d(eng.handle, kmap.ptr, _ptr(feats), _ptr(weight), _ptr(bias), _ptr(residual),
+                                    _ptr(out), ci, co, dt, epi, float(eps)), "sc_conv3d")
+    else:
+        hw = halo_wait
+        eng.check(eng.lib.sc_conv3d_halo(eng.handle, kmap.ptr, _ptr(feats), _ptr(weight), _ptr(bias),
+                                         _ptr(residual), _ptr(out), ci, co, dt, epi, float(eps),
+                                         ctypes.c_void_p(int(hw.flags)), int(hw.world), int(hw.rank),
+                                         int(hw.epoch) & 0xFFFFFFFF), "sc_conv3d_halo")
     return out
 
 
