@@ -51,11 +51,12 @@ def parse_args():
                     help="c5 on >1 GPU: SMs left to NCCL while the interior conv runs beside the halo exchange; "
                          "-1 (default): exchange first, then one conv over all owned outputs (faster at 2 GPUs, "
                          "where the exchange is 0.04 ms)")
-    ap.add_argument("--c5-exchange", choices=["nccl", "peer", "peer-conv-wait"], default="peer",
+    ap.add_argument("--c5-exchange", choices=["nccl", "peer", "peer-conv-wait", "peer-interior-first"],
+                    default="peer",
                     help="c5 on >1 GPU: halo exchange by the library's peer-memory push and wait kernels over NVLink, "
-                         "then the conv (peer, default); the same push, then one conv that runs its interior tiles "
-                         "first and waits for the peers inside its kernel (peer-conv-wait); or NCCL "
-                         "all_to_all_single (nccl)")
+                         "then the conv (peer, default); the same push, then the conv waiting for the peers inside "
+                         "its kernel before its first tile (peer-conv-wait) or, on the interior+boundary map, before "
+                         "its first boundary tile (peer-interior-first); or NCCL all_to_all_single (nccl)")
     ap.add_argument("--workload", choices=["c2", "c5", "table"], default="c2",
                     help="c2: BASELINE configs[1] (default, data-parallel across ranks); "
                          "c5: configs[4] 1024^3 Morton-sharded across ranks with NCCL halo exchange (strong scaling)")
@@ -403,12 +404,12 @@ def run_c5(args):
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     reserve = args.c5_reserve_sms  # SMs left to the NCCL kernels while the interior conv runs
     peer = None
-    in_kernel_wait = plan is not None and args.c5_exchange == "peer-conv-wait"
-    if in_kernel_wait:
+    in_kernel_wait = plan is not None and args.c5_exchange in ("peer-conv-wait", "peer-interior-first")
+    if plan is not None and args.c5_exchange == "peer-interior-first":
         kms = [pkg.concat_kmaps(km_i, km_b)]  # interior tiles, then boundary tiles
-    elif plan is not None and (reserve < 0 or args.c5_exchange == "peer"):
+    elif plan is not None and (reserve < 0 or args.c5_exchange.startswith("peer")):
         kms = [pkg.build_kmap(loc_c, n_out=n_own, engine=eng)]
-    if plan is not None and args.c5_exchange in ("peer", "peer-conv-wait"):
+    if plan is not None and args.c5_exchange.startswith("peer"):
         peer = S.PeerHaloExchange(plan, own_f, eng)
 
     def layer(ev=None):
@@ -490,7 +491,9 @@ def run_c5(args):
                    "halo_voxels_total": halo_total, "interior_voxels_total": int_total,
                    "step": ("halo push kernel over NVLink (peer memory), then one conv of all owned outputs that "
                             "runs its interior tiles first and waits for the peers' pushes inside the kernel before "
-                            "its boundary tiles" if in_kernel_wait else
+                            "its boundary tiles" if args.c5_exchange == "peer-interior-first" and world > 1 else
+                            "halo push kernel over NVLink (peer memory), then one conv of all owned outputs that "
+                            "waits for the peers' pushes inside the kernel before its first tile" if in_kernel_wait else
                             "halo exchange by peer-memory push/wait kernels over NVLink, then the conv of all "
                             "owned outputs" if peer is not None else
                             "halo exchange (NCCL all_to_all_single), then the conv of all owned outputs"
