@@ -249,7 +249,7 @@ __device__ __forceinline__ void epi_chunk(uint32_t tb, int c0, bool live, const 
   }
 }
 
-template <int KC, int BNMAX, int TPI, bool BF16>
+template <int KC, int BNMAX, int TPI, bool BF16, bool WAIT>
 __global__ void __launch_bounds__(kTcThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmB, const TcParams p) {
   using S = TcShape<KC, BNMAX, TPI>;
@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // a shared load issued after this thread's cp.async waits for those
     // copies to land and would serialise the pipeline.
     bool abort = false;
-    bool waited = p.wait_flags == nullptr;
+    bool waited = !WAIT;  // WAIT: the launch waits for a halo exchange (p.wait_flags)
     // gather-index prefetch: warp w loads active offsets j = w, w+4, ... (<= 7 each)
     int4 pre[7][TPI];
     auto load_idx = [&](int64_t item) {
@@ -382,7 +382,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       named_bar_sync(1, kProducers);  // idx_s holds this group's indices
       int cb;
       const int64_t g = item_group(item, cb);
-      if (!waited && min((g + 1) * TPI, p.num_tiles) > p.wait_tile) {
+      if (WAIT && !waited && min((g + 1) * TPI, p.num_tiles) > p.wait_tile) {
         halo_flags_wait_warp(p.wait_flags, p.wait_world, p.wait_rank, p.wait_epoch, p.err);
         waited = true;
       }
@@ -451,7 +451,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // The kernel ends only after the exchange has arrived, also when this
     // CTA gathered no halo row: the caller's next exchange may then reuse
     // the peers' buffers.
-    if (!waited) halo_flags_wait_warp(p.wait_flags, p.wait_world, p.wait_rank, p.wait_epoch, p.err);
+    if (WAIT && !waited) halo_flags_wait_warp(p.wait_flags, p.wait_world, p.wait_rank, p.wait_epoch, p.err);
     cp_async_wait_all();
     if (abort && pt == 0) {
       // Error exit: let weight copies already issued into our shared memory land.
@@ -995,7 +995,9 @@ sc_status launch_tc(Handle* h, const KMap* km, const void* feats, const void* we
                    static_cast<uint64_t>(km->K) * p.ci * 2, KC, p.bn, Z::kTma))
     return set_error(h, SC_ECUDA, "cuTensorMapEncodeTiled failed");
   p.num_items = ((p.num_tiles + TPI - 1) / TPI) * p.co_blocks;
-  auto kern = conv_tc_kernel<KC, BNMAX, TPI, BF16>;
+  // the wait is compiled only into launches that have one
+  auto kern = p.wait_flags ? conv_tc_kernel<KC, BNMAX, TPI, BF16, true>
+                           : conv_tc_kernel<KC, BNMAX, TPI, BF16, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
   if (e != cudaSuccess) return cuda_error(h, e, "conv smem attribute");
   const int64_t ctas = h->conv_ctas > 0 ? std::min(h->conv_ctas, h->num_sms) : h->num_sms;
