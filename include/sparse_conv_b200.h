@@ -179,7 +179,10 @@ SC_API sc_status sc_kmap_build_noalloc(sc_handle* h, const int32_t* coords, int6
  * Output j of `second` becomes output first.n_out + j.  The conv schedules
  * every tile of `second` after all tiles of `first`, and sc_conv3d_halo waits
  * for the halo exchange only before those.  Halo data of the parts is not
- * kept.  No counterpart in the reference (its conv runs on one device). */
+ * kept; the parts stay valid and may be freed.  `flags`: only
+ * SC_BUILD_DEFER_CHECK applies (without it the call waits for the copy and
+ * returns the parts' build status).  No counterpart in the reference (its
+ * conv runs on one device). */
 SC_API sc_status sc_kmap_concat(sc_handle* h, const sc_kmap* first, const sc_kmap* second, uint32_t flags,
                                 sc_kmap** out);
 

@@ -206,9 +206,12 @@ class PeerHaloExchange:
     other ranks' halo rows of the next region and waits until every other
     rank has filled this rank's halo (``sc_halo_push`` / ``sc_halo_wait``, on
     the current stream).  ``push()`` only stores and signals; the conv that
-    follows waits inside its kernel, before its first tile that reads a halo
-    row (``conv3d(..., halo_wait=...)`` on a map from ``concat_kmaps`` of the
-    interior and boundary outputs), so the interior tiles hide the exchange.
+    follows then waits inside its kernel, before its first tile that reads a
+    halo row (``conv3d(..., halo_wait=...)``, e.g. on a map from
+    ``concat_kmaps`` of the interior and boundary outputs).  On the 1024^3
+    workload that conv ran slower inside the multi-GPU step than
+    ``exchange()`` followed by a plain conv (8 GPUs: 0.243 vs 0.213 ms per
+    layer), so ``exchange()`` is the faster path today.
     The caller keeps the owned rows of the region it exchanges in place
     (``region(parity)[:n_own]``); both regions start with the owned features
     given to the constructor.  Collective: all ranks build it together and
