@@ -174,7 +174,7 @@ def cpu_reference_steps(w, steps, warmup):
 
 
 def run_reference(args):
-    rank, _, world = dist_env()
+    rank, _, _ = dist_env()
     if rank != 0:
         return 0
     w, _ = make_inputs(0)
@@ -378,7 +378,7 @@ def run_c5(args):
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    for attempt in range(2):  # the first pass warms the stream-ordered memory pool
+    for _ in range(2):  # the first pass warms the stream-ordered memory pool
       t0.record()
       if world > 1:
         part = S.MortonPartition.balanced(coords, world)

@@ -158,6 +158,7 @@ def test_sparse_conv3d_module_caches_map(pkg, oracle, cuda):
     assert torch.equal(y.feats, z.feats)
     out, km2 = pkg.sparse_conv3d_forward(f, c, conv.weight, conv.bias)
     assert torch.equal(out, y.feats)
+    assert torch.equal(km2.export(), km.export())  # the functional path builds the same map
 
 
 def test_dense_conv_invariant_on_gpu(pkg, oracle, cuda):

@@ -1,7 +1,9 @@
-"""Morton-range sharded conv on 2+ GPUs (NCCL halo exchange) against one GPU.
+"""Morton-range sharded conv on 2+ GPUs against one GPU.
 
-Each rank owns a Morton range, exchanges its halo with all_to_all_single over
-NCCL, builds its map with owned rows as outputs, and runs the tcgen05 conv.
+Each rank owns a Morton range, exchanges its halo (all_to_all_single over
+NCCL; the library's peer-memory push followed by its wait kernel or by a conv
+that waits inside its kernel), builds its map with owned rows as outputs, and
+runs the tcgen05 conv.
 Owned outputs must equal the single-GPU conv bit for bit: every output row
 sums the same offsets in the same order, and offsets a tile skips add zeros.
 Skipped unless at least two GPUs are visible.
@@ -10,7 +12,6 @@ import os
 import socket
 import sys
 
-import numpy as np
 import pytest
 import torch
 import torch.multiprocessing as mp
