@@ -126,12 +126,16 @@ sc_status sc_create(sc_handle** out, const sc_config* cfg) {
     return SC_EUNSUPPORTED;
   }
   h->impl.num_sms = prop.multiProcessorCount;
+  // The zeroing runs on the legacy stream; wait for it so that kernels on a
+  // non-blocking caller stream never see the error word before it is zero.
   if (cudaMalloc(reinterpret_cast<void**>(&h->impl.derr), 16) != cudaSuccess ||
-      cudaMemset(h->impl.derr, 0, 16) != cudaSuccess) {
+      cudaMemset(h->impl.derr, 0, 16) != cudaSuccess || cudaStreamSynchronize(cudaStreamLegacy) != cudaSuccess) {
+    if (h->impl.derr) cudaFree(h->impl.derr);
     delete h;
     return SC_ECUDA;
   }
-  // Keep freed stream-ordered allocations cached in the pool.
+  // Keep freed stream-ordered allocations cached in the pool (best effort:
+  // without it the pool only releases memory sooner).
   cudaMemPool_t pool;
   if (cudaDeviceGetDefaultMemPool(&pool, c.device) == cudaSuccess) {
     uint64_t thr = ~0ull;

@@ -8,7 +8,8 @@
 // system-scope release.  sc_halo_wait polls this rank's flag words until all
 // peers have published the epoch; the wait is bounded (one second, then
 // SC_ETIMEOUT in the handle's device error word).  The conv that follows on
-// the same stream reads the halo rows.  A rank never runs more than one
+// the same stream reads the halo rows; sc_conv3d_halo instead waits inside the
+// conv kernel (sc_conv_tc.cu).  A rank never runs more than one
 // exchange ahead of a peer (it waits for the peer's rows of the current
 // exchange), so alternating two halo regions per step keeps a peer's reads
 // and this rank's writes apart.
@@ -83,7 +84,9 @@ sc_status peer_alloc(Handle* h, size_t bytes, void** ptr, void* ipc_handle_out) 
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, bytes);
   if (e != cudaSuccess) return cuda_error(h, e, "peer buffer allocation");
+  // zero (flag words included) before any peer can open the buffer
   e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamLegacy);
   cudaIpcMemHandle_t hd;
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&hd, p);
   if (e != cudaSuccess) {
@@ -111,9 +114,15 @@ sc_status halo_push(Handle* h, const void* feats, int row_bytes, const int32_t* 
                     const int64_t* dst_off, int64_t n_send, void* const* peer_bufs, uint32_t* const* peer_flags,
                     int world, int rank, uint32_t epoch) {
   if (!h->push_ticket) {
-    const cudaError_t e = cudaMalloc(&h->push_ticket, sizeof(unsigned int));
-    if (e != cudaSuccess) return cuda_error(h, e, "push ticket");
-    cudaMemset(h->push_ticket, 0, sizeof(unsigned int));
+    // zeroed on the stream the pushes run on, so the first push sees zero
+    // whatever kind of stream the caller uses
+    cudaError_t e = cudaMalloc(&h->push_ticket, sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemsetAsync(h->push_ticket, 0, sizeof(unsigned int), h->stream);
+    if (e != cudaSuccess) {
+      if (h->push_ticket) cudaFree(h->push_ticket);
+      h->push_ticket = nullptr;
+      return cuda_error(h, e, "push ticket");
+    }
   }
   const int64_t want = (n_send * (row_bytes / 16) + kPushThreads - 1) / kPushThreads;
   const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, 2 * h->num_sms)));
