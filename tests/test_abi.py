@@ -35,6 +35,12 @@ def test_null_arguments_are_rejected_without_touching_the_device(pkg):
     assert L.sc_destroy(None) == pkg._lib.SC_EINVAL
     assert L.sc_kmap_build(None, None, 0, 3, 1, 0, None) == pkg._lib.SC_EINVAL
     assert L.sc_conv3d(None, None, None, None, None, None, None, 1, 1, 1, 0, 0.0) == pkg._lib.SC_EINVAL
+    out = ctypes.c_void_p(1234)
+    assert L.sc_kmap_concat(None, None, None, 0, ctypes.byref(out)) == pkg._lib.SC_EINVAL
+    assert L.sc_conv3d_halo(None, None, None, None, None, None, None, 1, 1, 1, 0, 0.0, None, 2, 0, 1) == \
+        pkg._lib.SC_EINVAL
+    assert L.sc_halo_push(None, None, 16, None, None, None, 0, None, None, 2, 0, 1) == pkg._lib.SC_EINVAL
+    assert L.sc_halo_wait(None, None, 2, 0, 1) == pkg._lib.SC_EINVAL
     assert L.sc_last_error(None) == b"null handle"
     cfg = pkg._lib.ScConfig()
     L.sc_config_default(ctypes.byref(cfg))
