@@ -250,7 +250,8 @@ SC_API sc_status sc_halo_push(sc_handle* h, const void* feats, int32_t row_bytes
 
 /* sc_conv3d on a submanifold map whose gathers read halo rows filled by
  * sc_halo_push of exchange `epoch`: the conv waits on the device until word r
- * of `flags` is >= epoch for every r != rank, inside the conv kernel before
+ * of `flags` (4-byte aligned) is >= epoch for every r != rank, inside the
+ * conv kernel before
  * its first tile from the second part of a concatenated map (before its first
  * tile for other maps), so tiles that read no halo row run while the exchange
  * is in flight.  The conv finishes only after the exchange has arrived.  A
@@ -262,7 +263,8 @@ SC_API sc_status sc_conv3d_halo(sc_handle* h, const sc_kmap* km, const void* fea
                                 sc_dtype dtype, uint32_t epilogue, float ln_eps, const uint32_t* flags,
                                 int32_t world, int32_t rank, uint32_t epoch);
 
-/* Waits on the device until word r of `flags` (this rank's flag array) is
+/* Waits on the device until word r of `flags` (this rank's flag array, 4-byte
+ * aligned) is
  * >= epoch for every r != rank; a wait longer than one second records
  * SC_ETIMEOUT in the handle's device error word (see sc_synchronize) and
  * returns.  Enqueued on the handle's stream. */

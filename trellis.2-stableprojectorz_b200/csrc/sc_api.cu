@@ -210,8 +210,8 @@ sc_status sc_halo_push(sc_handle* h, const void* feats, int32_t row_bytes, const
 sc_status sc_halo_wait(sc_handle* h, const uint32_t* flags, int32_t world, int32_t rank, uint32_t epoch) {
   if (!h) return SC_EINVAL;
   Handle* H = &h->impl;
-  if (world < 2 || world > 32 || rank < 0 || rank >= world || !flags)
-    return sc::set_error(H, SC_EINVAL, "halo wait: need 2 <= world <= 32, 0 <= rank < world and flags");
+  if (world < 2 || world > 32 || rank < 0 || rank >= world || !flags || !sc::aligned(flags, 4))
+    return sc::set_error(H, SC_EINVAL, "halo wait: need 2 <= world <= 32, 0 <= rank < world and 4-byte aligned flags");
   sc::DeviceGuard g(H->device);
   return sc::halo_wait(H, flags, world, rank, epoch);
 }
@@ -438,8 +438,9 @@ sc_status sc_conv3d_halo(sc_handle* h, const sc_kmap* km, const void* feats, con
                          const void* residual, void* out, int32_t ci, int32_t co, sc_dtype dtype, uint32_t epilogue,
                          float ln_eps, const uint32_t* flags, int32_t world, int32_t rank, uint32_t epoch) {
   if (!h || !km) return SC_EINVAL;
-  if (world < 2 || world > 32 || rank < 0 || rank >= world || !flags)
-    return sc::set_error(&h->impl, SC_EINVAL, "conv halo wait: need 2 <= world <= 32, 0 <= rank < world and flags");
+  if (world < 2 || world > 32 || rank < 0 || rank >= world || !flags || !sc::aligned(flags, 4))
+    return sc::set_error(&h->impl, SC_EINVAL,
+                         "conv halo wait: need 2 <= world <= 32, 0 <= rank < world and 4-byte aligned flags");
   if (km->impl->kind != SC_KMAP_SUBM) return sc::set_error(&h->impl, SC_EINVAL, "map is not a submanifold map");
   sc::ConvWait w;
   w.flags = flags;
