@@ -7,17 +7,37 @@ Ci = Co = 128, f32 accumulation.  One step = kernel-map build (hash probe,
 neighbour-mask tile sort) + the fused tcgen05 conv, on inputs resident in HBM;
 L2 is flushed (256 MB write) between steps outside the timed events.
 
-Metric: active voxels per second (whole job; every rank runs its own replica
-of the workload, data-parallel, so scaling is weak).  Extra keys report the conv
-kernel's useful TFLOP/s (2*Ci*Co*M, M = valid (output, offset) pairs) against
-the measured bf16 peak, the map-build time, the end-to-end number through the
-public Python API with host buffers, a CPU baseline, and sampled clocks.
+* N = 1: the whole workload on one GPU.
+* N > 1 (default): the same workload strong-scaled over the ranks: Morton-range
+  partition and halo plan once per coord set (outside the timed steps, like
+  the reference's cached neighbour map), then per step every rank builds the
+  map of its owned outputs, exchanges the one-voxel halo of input features
+  over NVLink (peer-memory push/wait kernels) and runs the conv of its owned
+  outputs.  Outside the timed region every rank checks its owned outputs
+  against a one-GPU conv of the whole workload, bit for bit
+  (``sharded_parity``).  ``--replicas`` instead runs one independent replica
+  of the workload per rank (weak scaling, no exchange).
+* Every N also reports a ``c5`` block: BASELINE.json configs[4] (1024^3,
+  6.1M voxels, Ci = Co = 32) Morton-sharded the same way, one conv layer per
+  step with the map built once per coord set.
+
+Metric: active voxels per second over the whole job.  Extra keys report the
+conv kernel's useful TFLOP/s (2*Ci*Co*M, M = valid (output, offset) pairs)
+against the measured bf16 peak, the map-build time, the end-to-end number
+through the public Python API with host buffers, a CPU baseline, and sampled
+clocks.
 
 ``--impl reference`` times the CPU restatement of the reference path
 (flat-key sort + searchsorted map, 27 x gather-matmul-scatter conv on torch
-CPU with all host threads) on the same workload: the reference's own
-conv_none.py / hashmap_fallback.py are not in the reference tree, and its
+CPU with all host threads) on the same workload and config: the reference's
+own conv_none.py / hashmap_fallback.py are not in the reference tree, and its
 WGSL path needs WebGPU, which these machines do not have.
+
+Other workloads: ``--workload c3`` (configs[2]: 4 ResBlock shapes split
+data-parallel over the ranks by greedy LPT on voxel count), ``--workload c4``
+(configs[3]: 512^3 down -> subm -> up, Morton-sharded, halo exchange only for
+the coarse submanifold conv), ``--workload c5`` (configs[4] alone),
+``--workload table`` (every config on one GPU next to its CPU sample).
 """
 from __future__ import annotations
 
@@ -47,19 +67,26 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-steps", type=int, default=3, help="timed CPU-baseline steps (rank 0, N=1)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N>1: one independent replica of the workload per rank (weak scaling, no exchange) "
+                         "instead of the Morton-sharded strong-scaling run")
+    ap.add_argument("--no-c5", action="store_true", help="skip the c5 (1024^3) block of the default run")
+    ap.add_argument("--c5-steps", type=int, default=20, help="timed layer steps of the c5 block")
     ap.add_argument("--c5-reserve-sms", type=int, default=-1,
-                    help="c5 on >1 GPU: SMs left to NCCL while the interior conv runs beside the halo exchange; "
-                         "-1 (default): exchange first, then one conv over all owned outputs (faster at 2 GPUs, "
-                         "where the exchange is 0.04 ms)")
+                    help="c5 with --c5-exchange nccl on >1 GPU: SMs left to NCCL while the interior conv runs "
+                         "beside the halo exchange; -1 (default): exchange first, then one conv over all owned "
+                         "outputs")
     ap.add_argument("--c5-exchange", choices=["nccl", "peer", "peer-conv-wait", "peer-interior-first"],
                     default="peer",
-                    help="c5 on >1 GPU: halo exchange by the library's peer-memory push and wait kernels over NVLink, "
-                         "then the conv (peer, default); the same push, then the conv waiting for the peers inside "
-                         "its kernel before its first tile (peer-conv-wait) or, on the interior+boundary map, before "
-                         "its first boundary tile (peer-interior-first); or NCCL all_to_all_single (nccl)")
-    ap.add_argument("--workload", choices=["c2", "c5", "table"], default="c2",
-                    help="c2: BASELINE configs[1] (default, data-parallel across ranks); "
-                         "c5: configs[4] 1024^3 Morton-sharded across ranks with NCCL halo exchange (strong scaling)")
+                    help="sharded convs on >1 GPU: halo exchange by the library's peer-memory push and wait kernels "
+                         "over NVLink, then the conv (peer, default); the same push, then the conv waiting for the "
+                         "peers inside its kernel before its first tile (peer-conv-wait) or, on the "
+                         "interior+boundary map, before its first boundary tile (peer-interior-first); or NCCL "
+                         "all_to_all_single (nccl)")
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "table"], default="c2",
+                    help="c2: BASELINE configs[1] (default); c3: configs[2] ResBlock batch, data-parallel; "
+                         "c4: configs[3] down/subm/up, Morton-sharded; c5: configs[4] 1024^3, Morton-sharded; "
+                         "table: every config on one GPU")
     return ap.parse_args()
 
 
@@ -145,8 +172,24 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+L2_NOTE = "flushed between steps by a 256 MB write outside the timed events"
+
+
+def c2_config(w, world, pairs, replicas=False):
+    """The ``config`` object of the default workload; both arms print the same one."""
+    if world == 1:
+        par, step = "single GPU", "kernel-map build + conv"
+    elif replicas:
+        par, step = f"data-parallel x{world} (one replica of the workload per rank)", "kernel-map build + conv"
+    else:
+        par = f"Morton-range sharding x{world} (strong scaling)"
+        step = "owned-output kernel-map build + halo exchange + conv (partition and halo plan once per coord set)"
+    return {"workload": w.name, "voxels": w.n, "ci": w.ci, "co": w.co, "kernel": "3x3x3 submanifold",
+            "pairs": int(pairs), "step": step, "l2": L2_NOTE, "parallelism": par}
+
+
 def make_inputs(rank):
-    """configs[1] on every rank: N data-parallel replicas of the same seeded shape."""
+    """configs[1], the same seeded shape on every rank."""
     import numpy as np
     import __graft_entry__
     pkg = __graft_entry__.load_package()
@@ -155,14 +198,15 @@ def make_inputs(rank):
 
 
 def cpu_reference_steps(w, steps, warmup):
-    """Times the CPU restatement of the reference path on the full workload."""
+    """Times the CPU restatement of the reference path on the full workload;
+    returns (seconds per timed step, threads, valid pairs of the map)."""
     import torch
     from oracle import sparse_conv_ref as R
     torch.set_num_threads(os.cpu_count() or 1)
     coords = torch.from_numpy(w.coords)
     feats = torch.from_numpy(w.feats).to(torch.bfloat16).float()
     weight = torch.from_numpy(w.weight).to(torch.bfloat16).float()
-    times = []
+    times, pairs = [], 0
     for i in range(warmup + steps):
         t0 = time.perf_counter()
         km = R.torch_cpu_kmap(coords, w.spatial_shape)
@@ -170,36 +214,81 @@ def cpu_reference_steps(w, steps, warmup):
         dt = time.perf_counter() - t0
         if i >= warmup:
             times.append(dt)
-    return times, torch.get_num_threads()
+        pairs = int((km >= 0).sum())
+    return times, torch.get_num_threads(), pairs
 
 
 def run_reference(args):
-    rank, _, _ = dist_env()
+    """The reference arm: the CPU restatement of the reference path (the
+    reference's own conv_none.py / hashmap_fallback.py are absent), honouring
+    --steps / --warmup, with the same metric, unit and config as our arm."""
+    rank, _, world = dist_env()
     if rank != 0:
         return 0
     w, _ = make_inputs(0)
-    steps = max(1, min(args.steps, 5))
-    warm = max(1, min(args.warmup, 1))
-    times, cores = cpu_reference_steps(w, steps, warm)
+    steps, warm = max(1, args.steps), max(0, args.warmup)
+    times, cores, pairs = cpu_reference_steps(w, steps, warm)
     t = sum(times)
     value = w.n * len(times) / t
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": len(times), "warmup": warm, "ms_per_step": 1e3 * t / len(times), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": "weak" if world == 1 or args.replicas else "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded union of 6 ellipsoid shells at 256^3 (BASELINE configs[1])",
-        "config": {"workload": w.name, "voxels": w.n, "ci": w.ci, "co": w.co, "step": "kernel map + conv",
-                   "implementation": "CPU restatement (torch CPU: flat-key sort + searchsorted, "
-                                     "27 x index_select/matmul/index_add_)"},
+        "config": c2_config(w, world, pairs, args.replicas),
+        "implementation": "CPU restatement of conv_none.py + hashmap_fallback.py (torch CPU: flat-key sort + "
+                          "searchsorted map, 27 x index_select/matmul/index_add_ conv), all host threads; "
+                          "inputs rounded to bf16, computed in f32",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"full workload ({w.n} voxels), {len(times)} timed steps"},
+                         "sample": f"full workload ({w.n} voxels) per step, {len(times)} timed steps after "
+                                   f"{warm} warm-up"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
+def init_dist(dev, world, seconds=300):
+    if world == 1:
+        return None
+    import torch.distributed as dist
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=seconds), device_id=dev)
+    return dist
+
+
+def max_over_ranks(dist, dev, values):
+    import torch
+    if dist is None:
+        return list(values)
+    tt = torch.tensor(list(values), device=dev, dtype=torch.float64)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    return tt.tolist()
+
+
+def sum_over_ranks(dist, dev, values):
+    import torch
+    if dist is None:
+        return list(values)
+    tt = torch.tensor(list(values), device=dev, dtype=torch.float64)
+    dist.all_reduce(tt)
+    return tt.tolist()
+
+
+def roofline_conv(ci, co, pairs, conv_s, peaks, peak_src):
+    flops = 2.0 * ci * co * pairs
+    achieved = flops / conv_s / 1e12
+    peak = float(peaks["bf16_tflops"])
+    traffic = load_traffic()
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "peak_source": f"{peak_src} bf16_tflops (burst)", "kernel": "conv_tc_kernel",
+            "units": "2*Ci*Co*M useful flops per launch",
+            "traffic": (traffic or {}).get("dram_bytes_per_launch"),
+            "traffic_source": ((traffic or {}).get("source") or "no committed ncu capture")}
+
+
 def run_ours(args):
+    """Default workload.  N=1 or --replicas: the whole workload per rank; N>1:
+    strong scaling through the Morton-sharded path (run_sharded_c2)."""
     import numpy as np
     import torch
     import __graft_entry__
@@ -207,10 +296,9 @@ def run_ours(args):
     rank, local_rank, world = dist_env()
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    dist = init_dist(dev, world, 180)
+    if world > 1 and not args.replicas:
+        return run_sharded_c2(args, pkg, dist, rank, world, dev)
     peaks, peak_src = measured_peaks()
 
     w, coords_np = make_inputs(rank)
@@ -260,23 +348,11 @@ def run_ours(args):
     t_total = sum(e[0].elapsed_time(e[2]) for e in ev) / 1e3
     t_map = sum(e[0].elapsed_time(e[1]) for e in ev) / 1e3
     t_conv = sum(e[1].elapsed_time(e[2]) for e in ev) / 1e3
-    if dist is not None:
-        tt = torch.tensor([t_total, t_map, t_conv], device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_total, t_map, t_conv = tt.tolist()
-        nv = torch.tensor([w.n], device=dev, dtype=torch.float64)
-        dist.all_reduce(nv)
-        n_all = float(nv.item())
-    else:
-        n_all = float(w.n)
+    t_total, t_map, t_conv = max_over_ranks(dist, dev, [t_total, t_map, t_conv])
+    n_all = sum_over_ranks(dist, dev, [float(w.n)])[0]
     value = n_all * args.steps / t_total
-
-    # conv kernel roofline (useful flops only: padded tile rows earn nothing)
-    flops = 2.0 * w.ci * w.co * info["num_pairs"]
     conv_s = t_conv / args.steps
-    achieved = flops / conv_s / 1e12
-    peak = float(peaks["bf16_tflops"])
-    traffic = load_traffic()
+    roof = roofline_conv(w.ci, w.co, info["num_pairs"], conv_s, peaks, peak_src)
 
     # end to end through the public API with host buffers: HostConvPipeline runs
     # every step's H2D copy, map build + conv and D2H copy, overlapping the
@@ -297,11 +373,7 @@ def run_ours(args):
         pipe.submit(coords_h, feats_h, out_h)
     e1.record(pipe.s_out)
     pipe.synchronize()
-    t_e2e = e0.elapsed_time(e1) / 1e3
-    if dist is not None:
-        tt = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_e2e = float(tt.item())
+    t_e2e = max_over_ranks(dist, dev, [e0.elapsed_time(e1) / 1e3])[0]
     e2e_value = n_all * e2e_steps / t_e2e
     h2d = coords_h.numel() * 4 + feats_h.numel() * 2
     d2h = out_h.numel() * 2
@@ -309,10 +381,12 @@ def run_ours(args):
     o_chk = pkg.conv3d(pkg.build_kmap(coords, engine=eng), feats, weight)
     e2e_matches = bool(torch.equal(o_chk.cpu(), ref_out))
 
+    c5 = None if args.no_c5 else c5_block(args, pkg, dist, rank, world, dev, eng, peaks, peak_src)
+
     # CPU baseline (rank 0, single GPU only)
     cpu = None
     if rank == 0 and world == 1 and args.cpu_steps > 0:
-        times, cores = cpu_reference_steps(w, args.cpu_steps, 1)
+        times, cores, _ = cpu_reference_steps(w, args.cpu_steps, 1)
         cpu = {"value": w.n * len(times) / sum(times), "unit": UNIT, "cores": cores, "kind": "port",
                "sample": f"full workload ({w.n} voxels), {len(times)} timed steps after 1 warm-up, "
                          f"torch CPU restatement with {cores} threads"}
@@ -326,23 +400,19 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": 1e3 * t_total / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic: seeded union of 6 ellipsoid shells at 256^3 (BASELINE configs[1]); the same shape on every rank",
-        "config": {"workload": w.name, "voxels_per_rank": w.n, "ci": w.ci, "co": w.co, "kernel": "3x3x3 submanifold",
-                   "pairs": info["num_pairs"], "tile_pairs": info["tile_pairs"],
-                   "step": "kernel-map build (hash probe + mask-sorted tiles) + fused tcgen05 conv",
-                   "l2": "flushed between steps by a 256 MB write outside the timed events",
-                   "parallelism": f"data-parallel x{world} (one replica of the workload per rank)"},
+        "data": "synthetic: seeded union of 6 ellipsoid shells at 256^3 (BASELINE configs[1]); the same shape "
+                "on every rank",
+        "config": c2_config(w, world, info["num_pairs"], args.replicas),
+        "tile_pairs": info["tile_pairs"],
         "map_build_ms": 1e3 * t_map / args.steps, "conv_ms": 1e3 * conv_s,
-        "conv_tflops": achieved, "conv_pct_of_bf16_peak": 100.0 * achieved / peak,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "peak_source": f"{peak_src} bf16_tflops (burst)",
-                     "kernel": "conv_tc_kernel", "units": "2*Ci*Co*M useful flops per launch",
-                     "traffic": (traffic or {}).get("dram_bytes_per_launch")},
+        "conv_tflops": roof["achieved"], "conv_pct_of_bf16_peak": 100.0 * roof["frac"],
+        "roofline": roof,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e2e_steps, "matches_device_api": e2e_matches,
                 "api": "HostConvPipeline.submit: per step H2D of coords+feats from pinned memory, map build + conv, "
                        "D2H of the output; consecutive steps overlap on 3 streams (depth 3)"},
+        "c5": c5,
         "clocks": clk.summary(),
         "gpu_launches": launches,
     }
@@ -350,70 +420,217 @@ def run_ours(args):
     return 0
 
 
-def run_c5(args):
-    """one 1024^3 shape (6.1M voxels, Ci=Co=32) Morton-sharded over the ranks.
+def shard_setup(pkg, S, coords, feats, world, rank, eng, exchange="peer"):
+    """Morton partition, halo plan and (peer) exchange of one coord set: the
+    per-coord-set work, done once like the reference's cached neighbour map."""
+    part = S.MortonPartition.balanced(coords, world)
+    own = part.owned_rows(coords, rank)
+    own_c = coords.index_select(0, own).contiguous()
+    plan = S.build_halo_plan(own_c, part, rank, world)
+    loc_c = S.local_coords(plan, own_c)
+    own_f = feats.index_select(0, S.owned_local(plan, own)).contiguous()
+    peer = S.PeerHaloExchange(plan, own_f, eng) if exchange.startswith("peer") else None
+    return part, own, plan, loc_c, own_f, peer
 
-    Every rank generates the same seeded shape, keeps its Morton range, builds
-    its halo plan and owned-output map once (cached per coord set, as the
-    reference caches neighbour maps), then each timed step is one conv layer:
-    halo exchange (NCCL all_to_all_single) + conv on owned outputs.
-    """
+
+def run_sharded_c2(args, pkg, dist, rank, world, dev):
+    """configs[1] strong-scaled over the ranks (Morton ranges, one-voxel halo over NVLink)."""
     import torch
-    import __graft_entry__
-    pkg = __graft_entry__.load_package()
     from sparseconv_b200 import sharding as S
-    rank, local_rank, world = dist_env()
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     peaks, peak_src = measured_peaks()
-    w = pkg.workloads.make_workload(5)
+    w, coords_np = make_inputs(rank)
     eng = pkg.get_engine(dev)
+    coords = torch.from_numpy(coords_np).to(dev)
+    feats = torch.from_numpy(w.feats).to(dev, torch.bfloat16)
+    weight = torch.from_numpy(w.weight).to(dev, torch.bfloat16)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    part, own, plan, loc_c, own_f, peer = shard_setup(pkg, S, coords, feats, world, rank, eng)
+    t1.record()
+    torch.cuda.synchronize()
+    setup_ms = t0.elapsed_time(t1)
+    out = torch.empty((plan.n_own, w.co), dtype=torch.bfloat16, device=dev)
+
+    def step(ev=None):
+        if ev:
+            ev[0].record()
+        km = pkg.build_kmap(loc_c, n_out=plan.n_own, engine=eng, check=False)
+        if ev:
+            ev[1].record()
+        loc = peer.exchange()
+        if ev:
+            ev[2].record()
+        pkg.conv3d(km, loc, weight, out=out)
+        if ev:
+            ev[3].record()
+        return km
+
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        step().free()
+    torch.cuda.synchronize()
+    km = step()
+    km.check()
+    info = km.info()
+    eng.synchronize()
+    km.free()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    with ClockSampler(dev.index) as clk:
+        dist.barrier()
+        torch.cuda.synchronize()
+        launches0 = eng.launch_count()
+        for k in range(args.steps):
+            flush.zero_()
+            km = step(ev[k])
+            if k + 1 < args.steps:
+                km.free()
+        torch.cuda.synchronize()
+    launches = eng.launch_count() - launches0
+    km.check()
+    eng.synchronize()
+    km.free()
+    seg = [sum(e[i].elapsed_time(e[i + 1]) for e in ev) / 1e3 for i in range(3)]
+    t_total = sum(e[0].elapsed_time(e[3]) for e in ev) / 1e3
+    per_rank = [torch.zeros(1, device=dev, dtype=torch.float64) for _ in range(world)]
+    dist.all_gather(per_rank, torch.tensor([t_total], device=dev, dtype=torch.float64))
+    per_rank = [1e3 * float(x.item()) / args.steps for x in per_rank]
+    conv_rank0_s = seg[2] / args.steps
+    pairs_rank0 = info["num_pairs"]
+    t_total, t_map, t_exch, t_conv, setup_ms = max_over_ranks(dist, dev, [t_total] + seg + [setup_ms])
+    pairs_all, halo_all = sum_over_ranks(dist, dev, [float(info["num_pairs"]), float(plan.n_halo)])
+    value = w.n * args.steps / t_total
+
+    # bit-exact check of every rank's owned outputs against a one-GPU conv of the whole workload
+    full = pkg.conv3d(pkg.build_kmap(coords, engine=eng), feats, weight)
+    ok = torch.equal(out, full.index_select(0, own.index_select(0, plan.order)))
+    okt = torch.tensor([1 if ok else 0], device=dev, dtype=torch.int32)
+    dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+    parity = bool(okt.item())
+    del full
+
+    # end to end through the public API: per step H2D of this rank's owned
+    # coords and features from pinned memory, owned-output map build, halo
+    # exchange, conv, D2H of the owned outputs (the plan is per coord set)
+    own_c_h = loc_c[:plan.n_own].cpu().pin_memory()
+    own_f_h = own_f.cpu().pin_memory()
+    out_h = torch.empty((plan.n_own, w.co), dtype=torch.bfloat16).pin_memory()
+    loc_d = loc_c.clone()
+
+    def e2e_step():
+        loc_d[:plan.n_own].copy_(own_c_h, non_blocking=True)
+        peer.next_owned_rows().copy_(own_f_h, non_blocking=True)
+        k = pkg.build_kmap(loc_d, n_out=plan.n_own, engine=eng, check=False)
+        loc = peer.exchange()
+        pkg.conv3d(k, loc, weight, out=out)
+        out_h.copy_(out, non_blocking=True)
+        return k
+
+    for _ in range(3):
+        e2e_step().free()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, args.steps // 2)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step().free()
+    e1.record()
+    torch.cuda.synchronize()
+    t_e2e = max_over_ranks(dist, dev, [e0.elapsed_time(e1) / 1e3])[0]
+    e2e_ok = torch.equal(out_h, out.cpu())
+    h2d = own_c_h.numel() * 4 + own_f_h.numel() * 2
+    d2h = out_h.numel() * 2
+    h2d, d2h = sum_over_ranks(dist, dev, [float(h2d), float(d2h)])
+
+    c5 = None if args.no_c5 else c5_block(args, pkg, dist, rank, world, dev, eng, peaks, peak_src)
+    peer.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    roof = roofline_conv(w.ci, w.co, pairs_rank0, conv_rank0_s, peaks, peak_src)
+    roof["kernel"] = "conv_tc_kernel (rank 0's shard)"
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": 1e3 * t_total / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded union of 6 ellipsoid shells at 256^3 (BASELINE configs[1]), one shape "
+                "partitioned over the ranks",
+        "config": c2_config(w, world, int(pairs_all)),
+        "sharded_parity": parity,
+        "halo_voxels_total": int(halo_all), "setup_ms": setup_ms,
+        "map_build_ms": 1e3 * t_map / args.steps, "exchange_ms": 1e3 * t_exch / args.steps,
+        "conv_ms": 1e3 * t_conv / args.steps, "ms_per_step_by_rank": per_rank,
+        "phases": "map_build_ms / exchange_ms / conv_ms: max over ranks of each phase (peer push + wait kernels "
+                  "for the exchange)",
+        "roofline": roof,
+        "cpu_baseline": None,
+        "e2e": {"value": w.n * e2e_steps / t_e2e, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h), "steps": e2e_steps, "matches_device_api": bool(e2e_ok),
+                "api": "per rank and step: H2D of owned coords + features (pinned), build_kmap of owned outputs, "
+                       "PeerHaloExchange.exchange, conv3d, D2H of owned outputs; steps not overlapped"},
+        "c5": c5,
+        "clocks": clk.summary(),
+        "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def c5_block(args, pkg, dist, rank, world, dev, eng, peaks, peak_src):
+    """configs[4] (1024^3, 6.1M voxels, Ci = Co = 32) Morton-sharded over the
+    ranks: per coord set the partition, halo plan and owned-output map; per
+    layer step the halo exchange and the conv.  Returns a dict (every rank)."""
+    import torch
+    from sparseconv_b200 import sharding as S
+    w = pkg.workloads.make_workload(5)
     coords = torch.from_numpy(w.coords).to(dev)
     feats = torch.from_numpy(w.feats).to(dev, torch.bfloat16)
     weight = torch.from_numpy(w.weight).to(dev, torch.bfloat16)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    mode = args.c5_exchange
+    reserve = args.c5_reserve_sms
     n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for _ in range(2):  # the first pass warms the stream-ordered memory pool
-      t0.record()
-      if world > 1:
-        part = S.MortonPartition.balanced(coords, world)
-        own = part.owned_rows(coords, rank)
-        own_c = coords.index_select(0, own).contiguous()
-        plan = S.build_halo_plan(own_c, part, rank, world)
-        loc_c = S.local_coords(plan, own_c)
-        own_f = feats.index_select(0, S.owned_local(plan, own)).contiguous()
-        buf = torch.empty((plan.n_own + plan.n_halo, w.ci), dtype=torch.bfloat16, device=dev)
-        buf[:plan.n_own].copy_(own_f)
-        n_own, n_halo, n_int = plan.n_own, plan.n_halo, plan.n_interior
-        km_i = pkg.build_kmap(loc_c, n_out=n_int, engine=eng)
-        km_b = pkg.build_kmap(loc_c, out_begin=n_int, n_out=n_own - n_int, engine=eng)
-        kms = [km_i, km_b]
-      else:
-        plan, loc_c, buf, n_own, n_halo, n_int = None, coords, feats, w.n, 0, w.n
-        kms = [pkg.build_kmap(loc_c, engine=eng)]
-      t1.record()
-      torch.cuda.synchronize()
-      setup_ms = t0.elapsed_time(t1)
+        torch.cuda.synchronize()
+        t0.record()
+        if world > 1:
+            part, own, plan, loc_c, own_f, peer = shard_setup(pkg, S, coords, feats, world, rank, eng, mode)
+            n_own, n_int = plan.n_own, plan.n_interior
+            buf = torch.empty((plan.n_own + plan.n_halo, w.ci), dtype=torch.bfloat16, device=dev)
+            buf[:n_own].copy_(own_f)
+            if mode == "peer-interior-first":
+                kms = [pkg.concat_kmaps(pkg.build_kmap(loc_c, n_out=n_int, engine=eng),
+                                        pkg.build_kmap(loc_c, out_begin=n_int, n_out=n_own - n_int, engine=eng))]
+            elif mode == "nccl" and reserve >= 0:
+                kms = [pkg.build_kmap(loc_c, n_out=n_int, engine=eng),
+                       pkg.build_kmap(loc_c, out_begin=n_int, n_out=n_own - n_int, engine=eng)]
+            else:
+                kms = [pkg.build_kmap(loc_c, n_out=n_own, engine=eng)]
+        else:
+            plan, peer, buf, n_own, n_int = None, None, feats, w.n, w.n
+            kms = [pkg.build_kmap(coords, engine=eng)]
+        t1.record()
+        torch.cuda.synchronize()
+        setup_ms = t0.elapsed_time(t1)
+        if _ == 0 and world > 1:
+            if peer is not None:
+                peer.close()
+            del kms
     infos = [km.info() for km in kms]
     out = torch.empty((n_own, w.co), dtype=torch.bfloat16, device=dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    reserve = args.c5_reserve_sms  # SMs left to the NCCL kernels while the interior conv runs
-    peer = None
-    in_kernel_wait = plan is not None and args.c5_exchange in ("peer-conv-wait", "peer-interior-first")
-    if plan is not None and args.c5_exchange == "peer-interior-first":
-        kms = [pkg.concat_kmaps(km_i, km_b)]  # interior tiles, then boundary tiles
-    elif plan is not None and (reserve < 0 or args.c5_exchange.startswith("peer")):
-        kms = [pkg.build_kmap(loc_c, n_out=n_own, engine=eng)]
-    if plan is not None and args.c5_exchange.startswith("peer"):
-        peer = S.PeerHaloExchange(plan, own_f, eng)
+    in_kernel_wait = plan is not None and mode in ("peer-conv-wait", "peer-interior-first")
 
     def layer(ev=None):
-        """Halo exchange beside the interior conv, then the boundary conv."""
+        if plan is None:
+            if ev: ev[1].record()
+            pkg.conv3d(kms[0], buf, weight, out=out)
+            return
         if in_kernel_wait:
             loc, hw = peer.push()
             if ev: ev[1].record()
@@ -424,9 +641,8 @@ def run_c5(args):
             if ev: ev[1].record()
             pkg.conv3d(kms[0], loc, weight, out=out)
             return
-        if plan is None or reserve < 0:
-            if plan is not None:
-                S.exchange_halo(plan, buf[:n_own], out=buf)
+        if reserve < 0:
+            S.exchange_halo(plan, buf[:n_own], out=buf)
             if ev: ev[1].record()
             pkg.conv3d(kms[0], buf, weight, out=out)
             return
@@ -442,78 +658,333 @@ def run_c5(args):
         flush.zero_()
         layer()
     torch.cuda.synchronize()
+    steps = max(1, args.c5_steps)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for k in range(steps):
+        flush.zero_()
+        ev[k][0].record()
+        layer(ev[k])
+        ev[k][2].record()
+    torch.cuda.synchronize()
+    eng.synchronize()
+    t_total = sum(e[0].elapsed_time(e[2]) for e in ev) / 1e3
+    t_first = sum(e[0].elapsed_time(e[1]) for e in ev) / 1e3
+    t_last = sum(e[1].elapsed_time(e[2]) for e in ev) / 1e3
+    per_rank = [t_total]
+    if dist is not None:
+        allt = [torch.zeros(1, device=dev, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(allt, torch.tensor([t_total], device=dev, dtype=torch.float64))
+        per_rank = [float(x.item()) for x in allt]
+    t_total, t_first, t_last, setup_ms = max_over_ranks(dist, dev, [t_total, t_first, t_last, setup_ms])
+    halo_total, pairs, int_total = sum_over_ranks(
+        dist, dev, [float(plan.n_halo if plan is not None else 0), float(sum(i["num_pairs"] for i in infos)),
+                    float(n_int)])
+    if peer is not None:
+        peer.close()
+    ms = 1e3 * t_total / steps
+    feat_bytes = w.n * (w.ci + w.co) * 2
+    return {
+        "workload": w.name, "voxels": w.n, "ci": w.ci, "co": w.co, "pairs": int(pairs), "n_gpus": world,
+        "steps": steps, "value": w.n * steps / t_total, "unit": UNIT, "ms_per_step": ms,
+        "exchange_ms": 1e3 * t_first / steps, "conv_ms": 1e3 * t_last / steps,
+        "ms_per_step_by_rank": [1e3 * t / steps for t in per_rank], "setup_ms": setup_ms,
+        "halo_voxels_total": int(halo_total), "interior_voxels_total": int(int_total),
+        "exchange": "single GPU: none" if world == 1 else mode,
+        "step": "one conv layer (map built once per coord set)" + ("" if world == 1 else
+                                                                   " after the halo exchange of that layer"),
+        "phases": "exchange_ms = from step start to the conv launch (push + wait, or push only with an in-kernel "
+                  "wait); conv_ms = the conv",
+        "conv_tflops_total": 2.0 * w.ci * w.co * pairs / (t_total / steps) / 1e12,
+        "feature_gbs_total": feat_bytes / (t_total / steps) / 1e9,
+        "feature_frac_of_hbm": feat_bytes / (t_total / steps) / 1e9 / (float(peaks["hbm_gbs"]) * world),
+        "hbm_peak_source": f"{peak_src} hbm_gbs x n_gpus",
+    }
+
+
+def run_c5(args):
+    """configs[4] alone: one 1024^3 shape Morton-sharded over the ranks."""
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    rank, local_rank, world = dist_env()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = init_dist(dev, world, 300)
+    peaks, peak_src = measured_peaks()
+    eng = pkg.get_engine(dev)
+    args.c5_steps = args.steps
+    with ClockSampler(dev.index) as clk:
+        blk = c5_block(args, pkg, dist, rank, world, dev, eng, peaks, peak_src)
+    launches = eng.launch_count()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": blk["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": blk["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded union of 4 ellipsoid shells + 5% interior fill at 1024^3 (BASELINE configs[4])",
+        "config": {"workload": blk["workload"], "voxels": blk["voxels"], "ci": blk["ci"], "co": blk["co"],
+                   "pairs": blk["pairs"], "step": blk["step"], "l2": L2_NOTE,
+                   "parallelism": f"Morton-range sharding x{world}"},
+        "c5": blk,
+        "roofline": {"bound": "hbm", "achieved": blk["feature_gbs_total"],
+                     "peak": float(peaks["hbm_gbs"]) * world, "unit": "GB/s", "frac": blk["feature_frac_of_hbm"],
+                     "peak_source": blk["hbm_peak_source"],
+                     "units": "feature bytes in + out (N*(Ci+Co)*2) per layer step, summed over ranks"},
+        "clocks": clk.summary(), "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_c3(args):
+    """a batch of 4 ResBlock shapes (conv -> LN -> SiLU -> conv + skip,
+    256 channels) split data-parallel over the ranks by greedy LPT on voxel count;
+    weights replicated, no collective on the forward."""
+    import numpy as np
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from sparseconv_b200 import sharding as S
+    rank, local_rank, world = dist_env()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = init_dist(dev, world, 180)
+    peaks, peak_src = measured_peaks()
+    eng = pkg.get_engine(dev)
+    w = pkg.workloads.make_workload(3)
+    sizes = [int(np.sum(w.coords[:, 0] == b)) for b in range(w.batch_size)]
+    assign = S.lpt_assign(sizes, world)
+    mine = assign[rank]
+    coords_all = torch.from_numpy(w.coords).to(dev)
+    rows = S.batch_rows(coords_all, mine)
+    coords = coords_all.index_select(0, rows).contiguous()
+    feats_all = torch.from_numpy(w.feats).to(dev, torch.bfloat16)
+    feats = feats_all.index_select(0, rows).contiguous()
+    w1 = torch.from_numpy(w.weight).to(dev, torch.bfloat16)
+    w2 = torch.from_numpy(w.extra["weight2"]).to(dev, torch.bfloat16)
+    n = int(coords.shape[0])
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    h = torch.empty((max(n, 1), w.co), dtype=torch.bfloat16, device=dev)
+    out = torch.empty((max(n, 1), w.co), dtype=torch.bfloat16, device=dev)
+
+    def step(ev=None):
+        if ev: ev[0].record()
+        if n == 0:
+            if ev: ev[1].record(); ev[2].record()
+            return None
+        km = pkg.build_kmap(coords, engine=eng, check=False)
+        if ev: ev[1].record()
+        pkg.conv3d(km, feats, w1, silu=True, layernorm=True, out=h[:n])
+        pkg.conv3d(km, h[:n], w2, residual=feats, out=out[:n])
+        if ev: ev[2].record()
+        return km
+
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    km = step()
+    pairs = km.info()["num_pairs"] if km is not None else 0
+    eng.synchronize()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     with ClockSampler(dev.index) as clk:
-        # ranks leave the barrier together, after their samplers are running
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
         launches0 = eng.launch_count()
         for k in range(args.steps):
             flush.zero_()
-            ev[k][0].record()
-            layer(ev[k])
-            ev[k][2].record()
+            step(ev[k])
         torch.cuda.synchronize()
     launches = eng.launch_count() - launches0
     eng.synchronize()
-    if peer is not None:
-        peer.close()
     t_total = sum(e[0].elapsed_time(e[2]) for e in ev) / 1e3
-    t_first = sum(e[0].elapsed_time(e[1]) for e in ev) / 1e3  # exchange (+ interior conv when overlapped)
-    t_last = sum(e[1].elapsed_time(e[2]) for e in ev) / 1e3   # boundary conv
-    per_rank = [t_total]
+    t_map = sum(e[0].elapsed_time(e[1]) for e in ev) / 1e3
+    t_conv = sum(e[1].elapsed_time(e[2]) for e in ev) / 1e3
+    conv_rank_s = t_conv / args.steps
+    # bit-exact check against one GPU running the whole batch
+    ok = True
+    if n:
+        kf = pkg.build_kmap(coords_all, engine=eng)
+        hf = pkg.conv3d(kf, feats_all, w1, silu=True, layernorm=True)
+        of = pkg.conv3d(kf, hf, w2, residual=feats_all)
+        ok = torch.equal(out[:n], of.index_select(0, rows))
+    okt = torch.tensor([1 if ok else 0], device=dev, dtype=torch.int32)
+    if dist is not None:
+        dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+    per_rank = [1e3 * t_total / args.steps]
     if dist is not None:
         allt = [torch.zeros(1, device=dev, dtype=torch.float64) for _ in range(world)]
-        dist.all_gather(allt, torch.tensor([t_total], device=dev, dtype=torch.float64))
+        dist.all_gather(allt, torch.tensor([1e3 * t_total / args.steps], device=dev, dtype=torch.float64))
         per_rank = [float(x.item()) for x in allt]
-        tt = torch.tensor([t_total, t_first, t_last, setup_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_total, t_first, t_last, setup_ms = tt.tolist()
-        hh = torch.tensor([n_halo, sum(i["num_pairs"] for i in infos), n_int], device=dev, dtype=torch.float64)
-        dist.all_reduce(hh)
-        halo_total, pairs, int_total = int(hh[0]), int(hh[1]), int(hh[2])
+    t_total, t_map, t_conv = max_over_ranks(dist, dev, [t_total, t_map, t_conv])
+    pairs_all = sum_over_ranks(dist, dev, [float(pairs)])[0]
+    if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
-    else:
-        halo_total, pairs, int_total = 0, infos[0]["num_pairs"], w.n
     if rank != 0:
         return 0
-    value = w.n * args.steps / t_total
-    flops = 2.0 * w.ci * w.co * pairs
-    achieved_gbs = (w.n * (w.ci + w.co) * 2) / (t_total / args.steps) / 1e9  # all ranks together
+    roof = roofline_conv(w.ci, w.co, 2 * pairs, conv_rank_s, peaks, peak_src)
+    roof["kernel"] = "conv_tc_kernel (two convs of rank 0's batch elements)"
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": METRIC, "value": w.n * args.steps / t_total, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": 1e3 * t_total / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic: seeded union of 4 ellipsoid shells + 5% interior fill at 1024^3 (BASELINE configs[4])",
-        "config": {"workload": w.name, "voxels": w.n, "ci": w.ci, "co": w.co, "pairs": pairs,
-                   "halo_voxels_total": halo_total, "interior_voxels_total": int_total,
-                   "step": ("halo push kernel over NVLink (peer memory), then one conv of all owned outputs that "
-                            "runs its interior tiles first and waits for the peers' pushes inside the kernel before "
-                            "its boundary tiles" if args.c5_exchange == "peer-interior-first" and world > 1 else
-                            "halo push kernel over NVLink (peer memory), then one conv of all owned outputs that "
-                            "waits for the peers' pushes inside the kernel before its first tile" if in_kernel_wait else
-                            "halo exchange by peer-memory push/wait kernels over NVLink, then the conv of all "
-                            "owned outputs" if peer is not None else
-                            "halo exchange (NCCL all_to_all_single), then the conv of all owned outputs"
-                            if reserve < 0 or world == 1 else
-                            "halo exchange (NCCL all_to_all_single) beside the conv of interior outputs "
-                            f"(on {n_sms - reserve} of {n_sms} SMs), then the conv of boundary outputs") +
-                           "; plan and maps built once per coord set",
-                   "l2": "flushed between steps by a 256 MB write outside the timed events",
-                   "parallelism": f"Morton-range sharding x{world}"},
-        "setup_ms": setup_ms,
-        "phases": ("exchange_and_interior_ms = the push kernel, boundary_ms = the conv with its in-kernel wait"
-                   if in_kernel_wait else "exchange_and_interior_ms = exchange (+ interior conv when overlapped), "
-                   "boundary_ms = the conv after it"),
-        "exchange_and_interior_ms": 1e3 * t_first / args.steps,
-        "boundary_ms": 1e3 * t_last / args.steps, "ms_per_step_by_rank": [1e3 * t / args.steps for t in per_rank],
+        "data": "synthetic: 4 seeded ellipsoid shells at 128^3, one per batch element (BASELINE configs[2])",
+        "config": {"workload": w.name, "voxels": w.n, "batch": w.batch_size, "channels": w.ci,
+                   "pairs_per_conv": int(pairs_all),
+                   "step": "kernel-map build + conv(LN, SiLU) + conv(+skip)", "l2": L2_NOTE,
+                   "parallelism": f"data-parallel x{world}: batch elements by greedy LPT on voxel count",
+                   "assignment": assign, "voxels_per_batch_element": sizes},
+        "dp_parity": bool(okt.item()),
+        "map_build_ms": 1e3 * t_map / args.steps, "convs_ms": 1e3 * t_conv / args.steps,
+        "ms_per_step_by_rank": per_rank, "roofline": roof,
+        "clocks": clk.summary(), "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_c4(args):
+    """512^3 down (64->128) -> subm (128) -> up (128->64) Morton-sharded
+    over the ranks.  Boundaries are multiples of 8, so every 2x2x2 sibling group
+    (and so every parent) lives on one rank: down and up need no exchange; the
+    coarse submanifold conv exchanges a one-voxel coarse halo over NVLink.  The
+    maps and plans are built once per coord set (setup_ms); a step is the three
+    convs and the exchange."""
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from sparseconv_b200 import sharding as S
+    rank, local_rank, world = dist_env()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = init_dist(dev, world, 300)
+    peaks, peak_src = measured_peaks()
+    eng = pkg.get_engine(dev)
+    w = pkg.workloads.make_workload(4)
+    coords_all = torch.from_numpy(w.coords).to(dev)
+    feats_all = torch.from_numpy(w.feats).to(dev, torch.bfloat16)
+    wd = torch.from_numpy(w.weight).to(dev, torch.bfloat16)
+    ws = torch.from_numpy(w.extra["w_sub"]).to(dev, torch.bfloat16)
+    wu = torch.from_numpy(w.extra["w_up"]).to(dev, torch.bfloat16)
+    cmid = int(ws.shape[0])
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    if world > 1:
+        part = S.MortonPartition.balanced(coords_all, world)
+        own = part.owned_rows(coords_all, rank)
+    else:
+        part, own = None, torch.arange(w.n, device=dev)
+    fine = coords_all.index_select(0, own).contiguous()
+    f_own = feats_all.index_select(0, own).contiguous()
+    kd = pkg.build_down2(fine, engine=eng)
+    coarse = kd.out_coords()
+    ku = pkg.build_up2(kd)
+    peer = None
+    if world > 1:
+        plan = S.build_halo_plan(coarse, part.coarsen(), rank, world, interior_first=False)
+        loc_c = S.local_coords(plan, coarse)
+        peer = S.PeerHaloExchange(plan, torch.zeros((plan.n_own, cmid), dtype=torch.bfloat16, device=dev), eng)
+        ks = pkg.build_kmap(loc_c, n_out=plan.n_own, engine=eng)
+        halo = plan.n_halo
+    else:
+        ks = pkg.build_kmap(coarse, engine=eng)
+        halo = 0
+    t1.record()
+    torch.cuda.synchronize()
+    setup_ms = t0.elapsed_time(t1)
+    n_coarse = int(coarse.shape[0])
+    hd = torch.empty((n_coarse, cmid), dtype=torch.bfloat16, device=dev)
+    hs = torch.empty((n_coarse, cmid), dtype=torch.bfloat16, device=dev)
+    out = torch.empty((fine.shape[0], int(wu.shape[0])), dtype=torch.bfloat16, device=dev)
+
+    def chain(ev=None):
+        if ev: ev[0].record()
+        if peer is None:
+            pkg.conv3d(kd, f_own, wd, out=hd)
+            if ev: ev[1].record(); ev[2].record()
+            pkg.conv3d(ks, hd, ws, out=hs)
+        else:
+            pkg.conv3d(kd, f_own, wd, out=peer.next_owned_rows())
+            if ev: ev[1].record()
+            loc = peer.exchange()
+            if ev: ev[2].record()
+            pkg.conv3d(ks, loc, ws, out=hs)
+        pkg.conv3d(ku, hs, wu, out=out)
+        if ev: ev[3].record()
+
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        chain()
+    torch.cuda.synchronize()
+    eng.synchronize()
+    infos = [k.info() for k in (kd, ks, ku)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    with ClockSampler(dev.index) as clk:
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        launches0 = eng.launch_count()
+        for k in range(args.steps):
+            flush.zero_()
+            chain(ev[k])
+        torch.cuda.synchronize()
+    launches = eng.launch_count() - launches0
+    eng.synchronize()
+    seg = [sum(e[i].elapsed_time(e[i + 1]) for e in ev) / 1e3 for i in range(3)]
+    t_total = sum(e[0].elapsed_time(e[3]) for e in ev) / 1e3
+    per_rank = [1e3 * t_total / args.steps]
+    if dist is not None:
+        allt = [torch.zeros(1, device=dev, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(allt, torch.tensor([1e3 * t_total / args.steps], device=dev, dtype=torch.float64))
+        per_rank = [float(x.item()) for x in allt]
+    # bit-exact check against one GPU running the whole chain
+    kdf = pkg.build_down2(coords_all, engine=eng)
+    ksf = pkg.build_kmap(kdf.out_coords(), engine=eng)
+    kuf = pkg.build_up2(kdf)
+    of = pkg.conv3d(kuf, pkg.conv3d(ksf, pkg.conv3d(kdf, feats_all, wd), ws), wu)
+    ok = torch.equal(out, of.index_select(0, own))
+    okt = torch.tensor([1 if ok else 0], device=dev, dtype=torch.int32)
+    if dist is not None:
+        dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+    del of, kdf, ksf, kuf
+    t_total, t_down, t_exch, t_rest, setup_ms = max_over_ranks(dist, dev, [t_total] + seg + [setup_ms])
+    pairs = sum_over_ranks(dist, dev, [float(i["num_pairs"]) for i in infos] + [float(halo), float(n_coarse)])
+    flops = 2.0 * (64 * 128 * pairs[0] + 128 * 128 * pairs[1] + 128 * 64 * pairs[2])
+    if peer is not None:
+        peer.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": w.n * args.steps / t_total, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": 1e3 * t_total / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded union of 6 ellipsoid shells at 512^3 (BASELINE configs[3])",
+        "config": {"workload": w.name, "voxels": w.n, "coarse_voxels": int(pairs[4]),
+                   "pairs": {"down": int(pairs[0]), "subm": int(pairs[1]), "up": int(pairs[2])},
+                   "step": "down conv 64->128, coarse halo exchange, subm conv 128, up conv 128->64 "
+                           "(maps and plans once per coord set)",
+                   "l2": L2_NOTE, "parallelism": f"Morton-range sharding x{world}" if world > 1 else "single GPU"},
+        "sharded_parity": bool(okt.item()),
+        "halo_voxels_total": int(pairs[3]), "setup_ms": setup_ms,
+        "down_ms": 1e3 * t_down / args.steps, "exchange_ms": 1e3 * t_exch / args.steps,
+        "subm_up_ms": 1e3 * t_rest / args.steps, "ms_per_step_by_rank": per_rank,
         "conv_tflops_total": flops / (t_total / args.steps) / 1e12,
-        "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": float(peaks["hbm_gbs"]) * world,
-                     "unit": "GB/s", "frac": achieved_gbs / (float(peaks["hbm_gbs"]) * world),
-                     "peak_source": f"{peak_src} hbm_gbs x n_gpus",
-                     "units": "feature bytes in + out (N*(Ci+Co)*2) per layer step, summed over ranks"},
+        "conv_pct_of_bf16_peak_total": 100.0 * flops / (t_total / args.steps) / 1e12 /
+                                        (float(peaks["bf16_tflops"]) * world),
         "clocks": clk.summary(), "gpu_launches": launches,
     }
     print(json.dumps(line), flush=True)
@@ -645,6 +1116,10 @@ def main():
         return run_reference(args)
     if args.workload == "c5":
         return run_c5(args)
+    if args.workload == "c3":
+        return run_c3(args)
+    if args.workload == "c4":
+        return run_c4(args)
     if args.workload == "table":
         return run_table(args)
     return run_ours(args)

@@ -112,7 +112,10 @@ SC_API sc_status sc_set_stream(sc_handle* h, void* stream);
  * smaller grid leaves SMs free for a collective that runs beside the conv
  * (the halo exchange of a sharded conv).  No counterpart in the reference. */
 SC_API sc_status sc_set_conv_ctas(sc_handle* h, int32_t max_ctas);
-/* Waits for all work enqueued on the handle's stream. */
+/* Waits for all work enqueued on the handle's stream, then returns (and
+ * clears) the first error a kernel recorded in the handle's device error word
+ * since the last call: SC_ETIMEOUT (a bounded device wait ran out) or
+ * SC_EINVAL (sc_halo_push skipped a row with a bad destination). */
 SC_API sc_status sc_synchronize(sc_handle* h);
 /* Human-readable description of the last error on this handle. */
 SC_API const char* sc_last_error(const sc_handle* h);
@@ -167,8 +170,9 @@ SC_API sc_status sc_kmap_out_coords(sc_handle* h, const sc_kmap* km, int32_t* co
  * Scratch is a fixed 8 MiB __device__ array held by every GPU that loads the
  * library: n must be <= SC_NOALLOC_MAX_VOXELS (else SC_EINVAL).  Calls share
  * that scratch, so calls that overlap on the GPU race; order them.  The first
- * call on a device looks up the scratch address; make it before any stream
- * capture on that device.  Waits for the build and returns its status. */
+ * call on a device looks up the scratch address.  Every call waits for its
+ * build on the handle's stream and returns its status, so it cannot be made
+ * while that stream is being captured (SC_EINVAL, nothing enqueued). */
 #define SC_NOALLOC_MAX_VOXELS 131072
 SC_API sc_status sc_kmap_build_noalloc(sc_handle* h, const int32_t* coords, int64_t n, int32_t dilation,
                                        int32_t* map_out);
@@ -239,7 +243,11 @@ SC_API sc_status sc_peer_close(sc_handle* h, void* peer_ptr);
 /* Copies rows to other ranks and signals them: row k of the send list is
  * `feats` row src_row[k] (row_bytes bytes, a multiple of 16), stored at byte
  * offset dst_off[k] of peer buffer dst_peer[k] (peer_bufs: device array of
- * `world` buffer addresses).  When every row has been stored, writes `epoch`
+ * `world` buffer addresses).  dst_off[k] must be a non-negative multiple of
+ * 16 and dst_peer[k] in [0, world) and != rank; a row that breaks either rule
+ * is not stored and records SC_EINVAL in the handle's device error word (see
+ * sc_synchronize).  The caller keeps dst_off[k] + row_bytes within the
+ * destination's buffer.  When every row has been stored, writes `epoch`
  * to word `rank` of each peer's flag array (peer_flags: device array of
  * `world` flag-array addresses).  2 <= world <= 32.  Enqueued on the
  * handle's stream. */

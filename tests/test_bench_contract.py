@@ -17,15 +17,22 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def test_reference_arm_prints_one_contract_line():
-    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
-                        "--warmup", "1"], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "2",
+                        "--warmup", "0"], cwd=ROOT, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
     assert len(lines) == 1
     d = json.loads(lines[0])
     assert d["impl"] == "reference"
     assert d["unit"] == "voxels/s" and d["higher_is_better"] is True
-    assert d["value"] > 0 and d["steps"] == 1 and d["n_gpus"] == 1
+    # the arm honours --steps / --warmup and prints our arm's config object
+    assert d["value"] > 0 and d["steps"] == 2 and d["warmup"] == 0 and d["n_gpus"] == 1
+    sys.path.insert(0, ROOT)
+    import bench
+    import __graft_entry__
+    w = __graft_entry__.load_package().workloads.make_workload(2)
+    assert d["config"] == bench.c2_config(w, 1, d["config"]["pairs"])
+    assert d["config"]["pairs"] == 4679479  # valid (output, offset) pairs of the 256^3 workload's map
     assert d["config"]["workload"] and d["config"]["voxels"] > 0
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     cb = d["cpu_baseline"]

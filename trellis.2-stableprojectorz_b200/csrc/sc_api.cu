@@ -241,7 +241,10 @@ sc_status sc_synchronize(sc_handle* h) {
     cudaMemsetAsync(H->derr, 0, sizeof(int), H->stream);
     cudaStreamSynchronize(H->stream);
     return sc::set_error(H, static_cast<sc_status>(err),
-                         err == SC_ETIMEOUT ? "device wait limit expired in a conv kernel" : "conv kernel error");
+                         err == SC_ETIMEOUT ? "device wait limit expired in a conv kernel"
+                         : err == SC_EINVAL ? "a kernel rejected an argument (halo push destination out of range or "
+                                              "not 16-byte aligned)"
+                                            : "conv kernel error");
   }
   return SC_OK;
 }

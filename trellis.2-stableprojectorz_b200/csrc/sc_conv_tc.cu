@@ -3,20 +3,22 @@
 // Implicit GEMM over the kernel map: for each 128-row output tile and each
 // neighbour offset v present in the tile,
 //     D[128, bn] += gather(feats, gidx[t][v])[128, Ci] . W[:, v, :]^T
-// The gathered rows are copied with 16-byte cp.async by four producer warps
-// straight into the 128B/64B/32B-swizzled K-major layout (rows of -1 are
-// zero-filled); W[:, v, kc] arrives by a tiled TMA load.  tcgen05.mma reads
-// both from shared memory and accumulates in TMEM (two buffers, so the
-// epilogue of one tile overlaps the main loop of the next).  The epilogue adds
-// bias and optionally LayerNorm / SiLU / residual and stores bf16/f16 rows.
+// The gathered rows arrive by TMA row gathers (tile::gather4: four rows of
+// one K chunk per instruction, rows of -1 read as zeros) straight into the
+// 128B/64B/32B-swizzled K-major layout the MMA reads; W[:, v, kc] arrives by
+// a tiled TMA load into the same stage, and the stage completes by
+// transaction count.  tcgen05.mma reads both operands from shared memory and
+// accumulates in TMEM (two buffers, so the epilogue of one tile group
+// overlaps the main loop of the next).  The epilogue adds bias and
+// optionally LayerNorm / SiLU / residual and stores bf16/f16 rows.
 //
-// Warp roles (288 threads, one persistent CTA per SM):
-//   warps 0-3  producers: per tile, stage the tile's gather indices in shared
-//              memory (double-buffered, prefetched one tile ahead), then per
-//              (offset, K-chunk) stage issue the row copies; thread 0 also
-//              issues the weight TMA
-//   warp 4     TMEM allocator + single-thread MMA issuer
-//   warps 5-8  epilogue (warp w reads TMEM lanes 32*(w%4) .. +31)
+// Warp roles (416 threads, one persistent CTA per SM):
+//   warps 0-7  producers in two groups of four taking alternate (K chunk,
+//              offset) stages; within a group each lane issues one gather4
+//              per stage, quads with no row are zero-filled instead; the
+//              group leader also loads the weight tile
+//   warp 8     TMEM allocator + single-thread MMA issuer
+//   warps 9-12 epilogue (warp w reads TMEM lanes 32*(w%4) .. +31)
 //
 // Reference math: src/sparse/ops/conv3d_wgsl.ts:177-222 (pass 2), weight
 // layout (Co,Kd,Kh,Kw,Ci) from src/sparse/ops/conv3d.ts:5,48-49.  No TMA
@@ -103,10 +105,13 @@ __device__ __forceinline__ void halo_flags_wait_warp(const uint32_t* flags, int 
   __syncwarp();
 }
 
-constexpr int kProducers = 128;  // warps 0-3
-constexpr int kMmaWarp = 4;
-constexpr int64_t kWorkOrderMaxItemsPerCta = 64;
-constexpr int kTcThreads = 288;
+constexpr int kGroupWarps = 4;     // producer warps per group (one per SM sub-partition)
+constexpr int kGroups = 2;         // producer groups, taking alternate stages
+constexpr int kProducerWarps = kGroupWarps * kGroups;  // warps 0-7
+constexpr int kMmaWarp = 8;
+constexpr int kEpiWarp0 = 9;       // warps 9-12: epilogue
+constexpr int kIdxAhead = 4;  // stages whose gather indices a producer warp holds in registers
+constexpr int kTcThreads = (kEpiWarp0 + 4) * 32;
 
 // Shared-memory plan for one CTA.  A stage holds TPI gathered A tiles
 // (128 rows x KC each) and one weight tile (BNMAX rows x KC) that all TPI
@@ -117,9 +122,8 @@ struct TcShape {
   static constexpr int kBBytes = BNMAX * KC * 2;
   static constexpr int kStageBytes = TPI * kABytes + kBBytes;
   static constexpr int kOutBytes = 4 * 32 * 16 * 2;  // epilogue staging: per warp 32 rows x 16 columns
-  static constexpr int kIdxBytes = 27 * 128 * TPI * 4;  // gather indices of the tile group being produced
   static constexpr int kBarBytesPlan = 256, kAlignSlack = 1024;
-  static constexpr int kStageBudget = 227 * 1024 - kIdxBytes - kOutBytes - kBarBytesPlan - kAlignSlack;
+  static constexpr int kStageBudget = 227 * 1024 - kOutBytes - kBarBytesPlan - kAlignSlack;
   static constexpr int kStagesFit = kStageBudget / kStageBytes;
   static constexpr int kStages = kStagesFit > 12 ? 12 : kStagesFit;
   static_assert(kStages >= 2, "not enough shared memory for two stages");
@@ -128,7 +132,7 @@ struct TcShape {
       (2 * kAccCols <= 32) ? 32 : (2 * kAccCols <= 64) ? 64 : (2 * kAccCols <= 128) ? 128 : (2 * kAccCols <= 256) ? 256 : 512;
   static_assert(2 * kAccCols <= 512, "two accumulator buffers must fit in TMEM");
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kIdxBytes + kOutBytes + kBarBytes + 1024;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + kBarBytes + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory plan too large");
   static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment");
   static_assert(2 * kStages + 5 <= 30, "barrier area too small");
@@ -251,14 +255,13 @@ __device__ __forceinline__ void epi_chunk(uint32_t tb, int c0, bool live, const 
 
 template <int KC, int BNMAX, int TPI, bool BF16, bool WAIT>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap tmB, const TcParams p) {
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmF, const TcParams p) {
   using S = TcShape<KC, BNMAX, TPI>;
   using Z = SwizzleCfg<KC>;
   using T = std::conditional_t<BF16, __nv_bfloat16, __half>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  int32_t* idx_s = reinterpret_cast<int32_t*>(smem + S::kStages * S::kStageBytes);  // [27][TPI*128]
-  uint8_t* out_s = smem + S::kStages * S::kStageBytes + S::kIdxBytes;  // [4 warps][32 rows][16 cols]
+  uint8_t* out_s = smem + S::kStages * S::kStageBytes;  // [4 warps][32 rows][16 cols]
   uint64_t* bars = reinterpret_cast<uint64_t*>(out_s + S::kOutBytes);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 30);
   const uint32_t smem_base = smem_u32(smem);
@@ -272,7 +275,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::kStages; ++s) {
-      mbar_init(full0 + 8u * s, kProducers + 1);  // one cp.async arrival per producer + the weight TMA
+      // the stage's group leader arrives once; the TMA copies (and the
+      // leader, for the quads it zero-filled) complete the bytes
+      mbar_init(full0 + 8u * s, 1);
       mbar_init(empty0 + 8u * s, 1);
     }
     mbar_init(tfull0, 1);
@@ -282,6 +287,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_init(done_bar, 1);
     fence_mbar_init();
     prefetch_tmap(&tmB);
+    prefetch_tmap(&tmF);
   }
   if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(s_tmem), S::kTmemCols);
@@ -321,140 +327,158 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     return m;
   };
 
-  if (warp < kProducers / 32) {
+  // The stage sequence is (item, K chunk, active offset) with K chunks
+  // outermost, so every output row accumulates (chunk, offset) products in
+  // the same order in every conv kernel.  Both producer groups and the MMA
+  // issuer walk it; a Cursor is one position in it.
+  struct Cursor {
+    int64_t round, item, g;
+    int cb, kc, v;
+    uint32_t mask0, mask;
+  };
+  auto enter_item = [&](Cursor& c) {  // first stage of item >= c.round's, skipping items with no offsets
+    for (c.item = next_item(c.round); c.item >= 0; ++c.round, c.item = next_item(c.round)) {
+      c.g = item_group(c.item, c.cb);
+      c.mask0 = group_mask(c.g);
+      if (c.mask0) break;
+    }
+    if (c.item >= 0) {
+      c.kc = 0;
+      c.mask = c.mask0;
+      c.v = __ffs(c.mask) - 1;
+    }
+  };
+  auto advance = [&](Cursor& c) {
+    c.mask &= c.mask - 1u;
+    if (!c.mask) {
+      if (++c.kc < p.nchunks) {
+        c.mask = c.mask0;
+      } else {
+        ++c.round;
+        enter_item(c);
+        return;
+      }
+    }
+    c.v = __ffs(c.mask) - 1;
+  };
+
+  if (warp < kProducerWarps) {
     // ------------------------------------------------------------ producers
-    constexpr int CPR = KC / 8;             // 16-byte chunks per gathered row
-    constexpr int RSTEP = 128 / CPR;        // rows between one thread's copies
-    constexpr int ROWB = KC * 2;            // bytes per row in a stage
-    const int pt = threadIdx.x;             // 0..127
-    const int chunk = pt % CPR;
-    const int row0 = pt / CPR;
-    const T* feats = static_cast<const T*>(p.feats);
-    const uint32_t b_tx = static_cast<uint32_t>(bn * KC * 2);
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t used = 0, used_par = 0;  // stages whose weight TMA was issued, parity of the last issue
-    // A timed-out wait sets this warp's `abort`; the warp then keeps walking
-    // the same item sequence without waiting or copying, so the named barrier
-    // below is reached the same number of times by all four warps (the other
-    // warps time out on their own waits).  No shared-memory flag is polled:
-    // a shared load issued after this thread's cp.async waits for those
-    // copies to land and would serialise the pipeline.
+    // Two groups of four warps (one per SM sub-partition) take alternate
+    // stages: while one group waits for its ring slot and synchronises, the
+    // other issues, so the sub-partitions' TMA issue paths stay busy (one
+    // sub-partition issues a gather4 only every ~80 cycles; the SM's TMA unit
+    // takes one every ~19).  Within a group every stage is split over the
+    // four warps: warp w issues quads [w*QPW, (w+1)*QPW) of the stage's
+    // TPI*32 row quads from its first QPW lanes (one gather4 = four rows of
+    // one K chunk, rows of -1 read as zeros).  Per stage:
+    //   1. the group leader waits for the slot, posts every byte of the stage
+    //      (all quads + the weight tile) and loads the weight tile by TMA;
+    //   2. barrier 1 (OR of failures): all warps agree on an abort;
+    //   3. lanes issue a gather4 for every quad holding at least one row;
+    //      quads with none are zero-filled by the warp with shared stores and
+    //      fenced to the async proxy (21% of the quads on the 256^3 workload);
+    //   4. barrier 2 (count of zero-filled quads);
+    //   5. the leader completes the zero-filled quads' bytes itself and
+    //      arrives (release), so the MMA sees every byte and every zero store.
+    // Each warp loads its lanes' gather indices kIdxAhead of its group's
+    // stages ahead into a register ring (plain coalesced loads, no staging).
+    constexpr int ROWB = KC * 2;           // bytes per gathered row
+    constexpr int QB = 4 * ROWB;           // bytes per row quad
+    constexpr int QPW = TPI * 32 / kGroupWarps;  // row quads per warp and stage
+    const int grp = warp / kGroupWarps, gw = warp % kGroupWarps;
+    const uint32_t bar_id = 1u + static_cast<uint32_t>(grp);
+    const bool leader = gw == 0 && lane == 0;
+    const int quad_lin = gw * QPW + lane;  // this lane's quad (valid for lane < QPW)
+    const int my_tile = quad_lin >> 5, my_quad = quad_lin & 31;
+    const bool issuer = lane < QPW;
+    const uint32_t stage_tx = static_cast<uint32_t>(TPI * S::kABytes + bn * KC * 2);
+    auto load_idx = [&](const Cursor& c) -> int4 {
+      const int64_t t = c.g * TPI + my_tile;
+      return issuer && t < p.num_tiles
+                 ? __ldg(reinterpret_cast<const int4*>(p.gidx + (t * p.K + c.v) * kTileRows) + my_quad)
+                 : make_int4(-1, -1, -1, -1);
+    };
+    auto step = [&](Cursor& c) {  // this group's next stage
+      for (int k = 0; k < kGroups && c.item >= 0; ++k) advance(c);
+    };
+    Cursor cur{}, ahead{};
+    enter_item(cur);
+    for (int k = 0; k < grp && cur.item >= 0; ++k) advance(cur);
+    ahead = cur;
+    int4 ring[kIdxAhead];
+#pragma unroll
+    for (int d = 0; d < kIdxAhead; ++d) {
+      if (ahead.item >= 0) {
+        ring[d] = load_idx(ahead);
+        step(ahead);
+      }
+    }
+    int64_t sidx = grp;  // position of `cur` in the CTA's stage sequence
+    uint32_t used = 0, used_par = 0;  // leader: slots with a stage issued, parity of the last issue
     bool abort = false;
     bool waited = !WAIT;  // WAIT: the launch waits for a halo exchange (p.wait_flags)
-    // gather-index prefetch: warp w loads active offsets j = w, w+4, ... (<= 7 each)
-    int4 pre[7][TPI];
-    auto load_idx = [&](int64_t item) {
-      int cb_unused;
-      const int64_t g = item_group(item, cb_unused);
-      const uint32_t m = group_mask(g);
-      const int nact = __popc(m);
+    while (cur.item >= 0 && !abort) {
 #pragma unroll
-      for (int k = 0; k < 7; ++k) {
-        const int j = warp + 4 * k;
-        if (j < nact) {
-          const int v = __fns(m, 0, j + 1);
-#pragma unroll
-          for (int i = 0; i < TPI; ++i) {
-            const int64_t t = g * TPI + i;
-            pre[k][i] = t < p.num_tiles ? __ldg(reinterpret_cast<const int4*>(p.gidx + (t * p.K + v) * 128) + lane)
-                                        : make_int4(-1, -1, -1, -1);
-          }
+      for (int d = 0; d < kIdxAhead; ++d) {
+        if (cur.item < 0) break;
+        if (WAIT && !waited && min((cur.g + 1) * TPI, p.num_tiles) > p.wait_tile) {
+          halo_flags_wait_warp(p.wait_flags, p.wait_world, p.wait_rank, p.wait_epoch, p.err);
+          fence_proxy_async_global();  // the TMA reads below see the peers' rows
+          waited = true;
         }
-      }
-      return nact;
-    };
-    auto store_idx = [&](int nact) {
-      int4* dst = reinterpret_cast<int4*>(idx_s);
-#pragma unroll
-      for (int k = 0; k < 7; ++k) {
-        const int j = warp + 4 * k;
-        if (j < nact) {
-#pragma unroll
-          for (int i = 0; i < TPI; ++i) dst[(j * TPI + i) * 32 + lane] = pre[k][i];
-        }
-      }
-    };
-    int64_t round = 0;
-    int64_t item = next_item(round);
-    if (item >= 0) store_idx(load_idx(item));
-    while (item >= 0) {
-      named_bar_sync(1, kProducers);  // idx_s holds this group's indices
-      int cb;
-      const int64_t g = item_group(item, cb);
-      if (WAIT && !waited && min((g + 1) * TPI, p.num_tiles) > p.wait_tile) {
-        halo_flags_wait_warp(p.wait_flags, p.wait_world, p.wait_rank, p.wait_epoch, p.err);
-        waited = true;
-      }
-      int64_t round_next = round + 1;
-      const int64_t next = next_item(round_next);
-      const int nact_next = next >= 0 ? load_idx(next) : 0;
-      // K chunks outermost, offsets inside: every output row accumulates
-      // (chunk, offset) products in the same order in every conv kernel.
-      const uint32_t mask0 = group_mask(g);
-      for (int kc = 0; kc < p.nchunks; ++kc) {
-        uint32_t mask = mask0;
-        for (int j = 0; mask; ++j) {
-          const int v = __ffs(mask) - 1;
-          mask &= mask - 1;
-          // One shared load per tile: lane l reads the index of row
-          // RW*w + l%RW + (l/RW)*RSTEP, which is row row0 + c*RSTEP of the
-          // thread at lane c*RW + l/CPR; shuffles hand every thread its rows.
-          constexpr int RW = 32 / CPR;
-          int rows_idx[TPI][CPR];
-#pragma unroll
-          for (int i = 0; i < TPI; ++i) {
-            const int mine = idx_s[(j * TPI + i) * 128 + RW * warp + (lane % RW) + (lane / RW) * RSTEP];
-#pragma unroll
-            for (int c = 0; c < CPR; ++c) rows_idx[i][c] = __shfl_sync(0xffffffffu, mine, c * RW + lane / CPR);
-          }
-          int w = 0;
-          if (lane == 0 && !abort) w = mbar_wait(empty0 + 8u * stage, phase ^ 1u, p.err) ? 1 : 0;
-          if (!__all_sync(0xffffffffu, lane != 0 || w != 0)) {
-            abort = true;
-            continue;
-          }
-          const uint32_t sbase = smem_base + static_cast<uint32_t>(stage * S::kStageBytes);
-          if (pt == 0) {
-            mbar_arrive_expect_tx(full0 + 8u * stage, b_tx);
-            tma_load_2d(sbase + TPI * S::kABytes, &tmB, v * p.ci + kc * KC, cb * bn, full0 + 8u * stage);
+        const int stage = static_cast<int>(sidx % S::kStages);
+        const uint32_t phase = static_cast<uint32_t>((sidx / S::kStages) & 1);
+        const uint32_t sbase = smem_base + static_cast<uint32_t>(stage * S::kStageBytes);
+        const uint32_t fb = full0 + 8u * stage;
+        bool fail = false;
+        if (leader) {
+          fail = !mbar_wait(empty0 + 8u * stage, phase ^ 1u, p.err);
+          if (!fail) {
+            mbar_expect_tx(fb, stage_tx);
+            tma_load_2d(sbase + TPI * S::kABytes, &tmB, cur.v * p.ci + cur.kc * KC, cur.cb * bn, fb);
             used |= 1u << stage;
             used_par = (used_par & ~(1u << stage)) | (phase << stage);
           }
-#pragma unroll
-          for (int i = 0; i < TPI; ++i) {
-#pragma unroll
-            for (int c = 0; c < CPR; ++c) {
-              const int r = row0 + c * RSTEP;
-              const int src_row = rows_idx[i][c];
-              const uint32_t o = static_cast<uint32_t>(r * ROWB + chunk * 16);
-              const uint32_t sw = o ^ (((o >> 7) & static_cast<uint32_t>(CPR - 1)) << 4);
-              const T* src =
-                  src_row >= 0 ? feats + static_cast<int64_t>(src_row) * p.ci + kc * KC + chunk * 8 : feats;
-              cp_async16(sbase + i * S::kABytes + sw, src, src_row >= 0 ? 16u : 0u);
-            }
-          }
-          cp_async_arrive_noinc(full0 + 8u * stage);
-          if (++stage == S::kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
         }
+        if (named_bar_red_or(bar_id, kGroupWarps * 32, fail)) {
+          abort = true;
+          break;
+        }
+        const int4 r4 = ring[d];
+        const bool empty_quad = issuer && (r4.x & r4.y & r4.z & r4.w) == -1;
+        const uint32_t qdst = sbase + my_tile * S::kABytes + my_quad * QB;
+        if (issuer && !empty_quad) tma_gather4(qdst, &tmF, cur.kc * KC, r4.x, r4.y, r4.z, r4.w, fb);
+        uint32_t zmask = __ballot_sync(0xffffffffu, empty_quad);
+        const bool any_zero = zmask != 0u;
+        while (zmask) {  // the warp zero-fills each empty quad: 16 bytes per lane
+          const int q = __ffs(zmask) - 1;
+          zmask &= zmask - 1u;
+          const uint32_t zdst = __shfl_sync(0xffffffffu, qdst, q);
+          if (lane * 16 < QB)
+            asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(zdst + lane * 16u), "r"(0u) : "memory");
+        }
+        if (any_zero) fence_proxy_async_smem();
+        const uint32_t nzero = named_bar_red_popc(bar_id, kGroupWarps * 32, empty_quad);
+        if (leader) {
+          if (nzero) mbar_complete_tx(fb, nzero * QB);
+          mbar_arrive(fb);
+        }
+        if (ahead.item >= 0) {
+          ring[d] = load_idx(ahead);
+          step(ahead);
+        }
+        step(cur);
+        sidx += kGroups;
       }
-      if (next >= 0) {
-        named_bar_sync(1, kProducers);  // every producer has read this group's indices
-        store_idx(nact_next);
-      }
-      round = round_next;
-      item = next;
     }
     // The kernel ends only after the exchange has arrived, also when this
     // CTA gathered no halo row: the caller's next exchange may then reuse
     // the peers' buffers.
     if (WAIT && !waited) halo_flags_wait_warp(p.wait_flags, p.wait_world, p.wait_rank, p.wait_epoch, p.err);
-    cp_async_wait_all();
-    if (abort && pt == 0) {
-      // Error exit: let weight copies already issued into our shared memory land.
+    if (abort && leader) {
+      // Error exit: let the copies already issued into our shared memory land
+      // (every stage's copies, from all warps of the group, complete one barrier).
       for (int s = 0; s < S::kStages; ++s)
         if (used & (1u << s)) mbar_wait(full0 + 8u * s, (used_par >> s) & 1u, nullptr);
     }
@@ -479,10 +503,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ok = false;
             break;
           }
-          // The rows were written by cp.async and signalled through
-          // cp.async.mbarrier.arrive; like CUTLASS's sm100 cp.async mainloop,
-          // no extra proxy fence is placed here (a consumer-side
-          // fence.proxy.async serialises the pipeline on all in-flight copies).
+          // The stage's rows arrived by TMA (async proxy, counted in the
+          // barrier's bytes) and by cp.async, whose threads fenced their
+          // landed copies to the async proxy before arriving (release); the
+          // barrier wait acquires both.
           tc_fence_after();
           const uint32_t a0 = smem_base + static_cast<uint32_t>(stage * S::kStageBytes);
           const uint32_t b0 = a0 + TPI * S::kABytes;
@@ -508,14 +532,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_wait(done_bar, 0, p.err);
     }
     __syncwarp();
-  } else {
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const T* bias = static_cast<const T*>(p.bias);
     const T* res = static_cast<const T*>(p.residual);
     T* out = static_cast<T*>(p.out);
-    uint8_t* wbuf = out_s + (warp - (kMmaWarp + 1)) * (32 * 32);
+    uint8_t* wbuf = out_s + (warp - kEpiWarp0) * (32 * 32);
     uint32_t it = 0;
     int64_t round = 0;
     for (int64_t item = next_item(round); item >= 0; ++round, item = next_item(round), ++it) {
@@ -989,10 +1013,12 @@ template <int KC, int BNMAX, int TPI, bool BF16>
 sc_status launch_tc(Handle* h, const KMap* km, const void* feats, const void* weight, TcParams p) {
   using S = TcShape<KC, BNMAX, TPI>;
   using Z = SwizzleCfg<KC>;
-  CUtensorMap tb;
+  CUtensorMap tb, tf;
   p.feats = feats;
+  // weights: [Co, K*Ci], box KC x bn; features: [n_in, Ci], box KC x 1 (row gathers)
   if (!make_map_2d(&tb, BF16, weight, static_cast<uint64_t>(km->K) * p.ci, p.co,
-                   static_cast<uint64_t>(km->K) * p.ci * 2, KC, p.bn, Z::kTma))
+                   static_cast<uint64_t>(km->K) * p.ci * 2, KC, p.bn, Z::kTma) ||
+      !make_map_2d(&tf, BF16, feats, p.ci, km->n_in, static_cast<uint64_t>(p.ci) * 2, KC, 1, Z::kTma))
     return set_error(h, SC_ECUDA, "cuTensorMapEncodeTiled failed");
   p.num_items = ((p.num_tiles + TPI - 1) / TPI) * p.co_blocks;
   // the wait is compiled only into launches that have one
@@ -1005,14 +1031,9 @@ sc_status launch_tc(Handle* h, const KMap* km, const void* feats, const void* we
   // Work order balances CTAs that run few items (10 per CTA on the 256^3
   // workload: -9% conv time); with many items per CTA static striding is
   // already balanced and the natural tile order keeps better L2 locality.
-  p.group_order = nullptr;
-  if (p.num_items < kWorkOrderMaxItemsPerCta * grid) {
-    const sc_status st = ensure_group_order(h, km, TPI);
-    if (st != SC_OK) return st;
-    p.group_order = km->group_order[TPI - 1];
-  }
+  p.group_order = p.num_items < kWorkOrderMaxItemsPerCta * grid ? km->group_order[TPI - 1] : nullptr;
   ++h->launches;
-  kern<<<static_cast<unsigned>(grid), kTcThreads, S::kSmemBytes, h->stream>>>(tb, p);
+  kern<<<static_cast<unsigned>(grid), kTcThreads, S::kSmemBytes, h->stream>>>(tb, tf, p);
   e = cudaGetLastError();
   return e == cudaSuccess ? SC_OK : cuda_error(h, e, "conv launch");
 }
@@ -1102,11 +1123,7 @@ sc_status launch_halo(Handle* h, const KMap* km, const void* feats, const void* 
   p.err = h->derr;
   const int64_t ctas = h->conv_ctas > 0 ? std::min(h->conv_ctas, h->num_sms) : h->num_sms;
   const int64_t grid = std::min<int64_t>(p.num_tiles, ctas);
-  if (p.num_tiles < kWorkOrderMaxItemsPerCta * grid) {
-    const sc_status st = ensure_group_order(h, km, 1);
-    if (st != SC_OK) return st;
-    p.group_order = km->group_order[0];
-  }
+  p.group_order = p.num_tiles < kWorkOrderMaxItemsPerCta * grid ? km->group_order[0] : nullptr;
   auto kern = conv_halo_kernel<BF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kHaloSmemBytes);
   if (e != cudaSuccess) return cuda_error(h, e, "halo conv smem attribute");

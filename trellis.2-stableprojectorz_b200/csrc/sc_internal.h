@@ -9,6 +9,10 @@ namespace sc {
 
 // Output rows are processed in tiles of this many rows (one TMEM lane each).
 constexpr int kTileRows = 128;
+// Convs with fewer items (tile groups x output-channel blocks) per CTA than
+// this take them in the map's work order; more items per CTA keep the
+// natural tile order (already balanced, better L2 locality).
+constexpr int64_t kWorkOrderMaxItemsPerCta = 64;
 
 struct Handle {
   int device = 0;
@@ -44,9 +48,9 @@ struct KMap {
   uint32_t* tile_mask = nullptr;
   // Groups of TPI = 1, 2 consecutive tiles ordered by descending work (number
   // of offsets the group runs); the conv schedules its items in this order.
-  // Filled on first use by a conv that needs it (ensure_group_order).
-  mutable int32_t* group_order[2] = {nullptr, nullptr};
-  mutable bool group_order_ready[2] = {false, false};
+  // Built with the map, on its stream, when a conv could use it (fewer than
+  // kWorkOrderMaxItemsPerCta * num_sms groups); null otherwise.
+  int32_t* group_order[2] = {nullptr, nullptr};
   // Halo tiles (SC_BUILD_HALO): tiles are output rows in order; per tile the
   // distinct input rows its gathers read (kHaloCap slots, padded with -1 to a
   // multiple of 4) and per (tile, offset, slot) the position of the gathered
@@ -76,7 +80,6 @@ sc_status build_down2(Handle* h, const int32_t* coords, int64_t n, uint32_t flag
 sc_status build_up2(Handle* h, const KMap* down, uint32_t flags, KMap** out);
 sc_status export_map(Handle* h, const KMap* km, int32_t* map_out);
 // allocation-free map build into caller memory (sc_noalloc.cu)
-sc_status ensure_group_order(Handle* h, const KMap* km, int tpi);
 // peer-memory halo exchange
 sc_status peer_alloc(Handle* h, size_t bytes, void** ptr, void* ipc_handle_out);
 sc_status peer_open(Handle* h, const void* ipc_handle, void** peer_ptr);

@@ -581,34 +581,42 @@ __device__ __forceinline__ int group_bucket(const uint32_t* tile_mask, int64_t g
   return 32 - __popc(m) + (end > split ? 33 : 0);  // more offsets first, late class last
 }
 
-__global__ void k_group_hist(const uint32_t* __restrict__ tile_mask, int64_t num_tiles, int tpi, int64_t groups,
-                             int64_t split, uint32_t* hist) {
-  __shared__ uint32_t sh[kWorkBuckets];
-  for (int b = threadIdx.x; b < kWorkBuckets; b += blockDim.x) sh[b] = 0;
-  __syncthreads();
-  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
-       g += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    atomicAdd(&sh[group_bucket(tile_mask, g, num_tiles, tpi, split)], 1u);
-  __syncthreads();
-  for (int b = threadIdx.x; b < kWorkBuckets; b += blockDim.x)
-    if (sh[b]) atomicAdd(&hist[b], sh[b]);
-}
+// Both work orders (groups of one and of two tiles) in one single-CTA
+// launch: bucket counts in shared memory, an exclusive scan turns them into
+// placement cursors, and a second pass places every group.  An order is
+// written only where its pointer is non-null.
+constexpr int kOrderThreads = 1024;
 
-__global__ void k_group_place(const uint32_t* __restrict__ tile_mask, int64_t num_tiles, int tpi, int64_t groups,
-                              int64_t split, const uint32_t* __restrict__ hist, uint32_t* cursor, int32_t* order) {
-  __shared__ uint32_t base[kWorkBuckets];
-  if (threadIdx.x == 0) {
+__global__ void __launch_bounds__(kOrderThreads) k_group_orders(const uint32_t* __restrict__ tile_mask,
+                                                                int64_t num_tiles, int64_t split, int32_t* order1,
+                                                                int32_t* order2) {
+  __shared__ uint32_t cur[2][kWorkBuckets];
+  for (int b = threadIdx.x; b < 2 * kWorkBuckets; b += blockDim.x) cur[b / kWorkBuckets][b % kWorkBuckets] = 0;
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    if (!(k ? order2 : order1)) continue;
+    const int64_t groups = (num_tiles + k) / (k + 1);
+    for (int64_t g = threadIdx.x; g < groups; g += blockDim.x)
+      atomicAdd(&cur[k][group_bucket(tile_mask, g, num_tiles, k + 1, split)], 1u);
+  }
+  __syncthreads();
+  if (threadIdx.x < 2) {
     uint32_t acc = 0;
     for (int b = 0; b < kWorkBuckets; ++b) {
-      base[b] = acc;
-      acc += hist[b];
+      const uint32_t c = cur[threadIdx.x][b];
+      cur[threadIdx.x][b] = acc;
+      acc += c;
     }
   }
   __syncthreads();
-  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
-       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int b = group_bucket(tile_mask, g, num_tiles, tpi, split);
-    order[base[b] + atomicAdd(&cursor[b], 1u)] = static_cast<int32_t>(g);
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    int32_t* order = k ? order2 : order1;
+    if (!order) continue;
+    const int64_t groups = (num_tiles + k) / (k + 1);
+    for (int64_t g = threadIdx.x; g < groups; g += blockDim.x)
+      order[atomicAdd(&cur[k][group_bucket(tile_mask, g, num_tiles, k + 1, split)], 1u)] = static_cast<int32_t>(g);
   }
 }
 
@@ -717,6 +725,29 @@ sc_status build_halo(Handle* h, KMap* km, const int32_t* map) {
   return SC_OK;
 }
 
+// Work orders of the conv's scheduler, built with the map on its stream so
+// that whatever is ordered after the build (any stream, any handle) sees
+// them.  A conv uses the order of its tiles-per-item count only when it runs
+// fewer than kWorkOrderMaxItemsPerCta items per CTA, and it runs at least one
+// item per group, so orders of kWorkOrderMaxItemsPerCta * num_sms groups or
+// more are never read and are not built.
+sc_status build_group_orders(Handle* h, KMap* km) {
+  if (km->num_tiles == 0) return SC_OK;
+  const int64_t split = km->split_tile >= 0 ? km->split_tile : km->num_tiles;
+  for (int t = 0; t < 2; ++t) {
+    const int64_t groups = (km->num_tiles + t) / (t + 1);
+    if (groups < kWorkOrderMaxItemsPerCta * h->num_sms)
+      SC_TRY_CUDA(dev_alloc(h, reinterpret_cast<void**>(&km->group_order[t]), sizeof(int32_t) * groups),
+                  "alloc group order");
+  }
+  if (!km->group_order[0] && !km->group_order[1]) return SC_OK;
+  ++h->launches;
+  k_group_orders<<<1, kOrderThreads, 0, h->stream>>>(km->tile_mask, km->num_tiles, split, km->group_order[0],
+                                                      km->group_order[1]);
+  SC_TRY_CUDA(cudaGetLastError(), "group order launch");
+  return SC_OK;
+}
+
 sc_status finish_tiles(Handle* h, KMap* km, const int32_t* map, uint32_t* row_mask, uint32_t flags, Temps& tmp) {
   const int64_t n = km->n_out;
   if (n == 0) return SC_OK;
@@ -751,7 +782,7 @@ sc_status finish_tiles(Handle* h, KMap* km, const int32_t* map, uint32_t* row_ma
   k_build_tiles<<<static_cast<unsigned>(km->num_tiles), kTileRows, 0, h->stream>>>(
       map, km->K, order, n, row_mask, km->gidx, km->tile_rows, km->tile_mask, km->counters);
   SC_TRY_CUDA(cudaGetLastError(), "tile build launch");
-  return SC_OK;
+  return build_group_orders(h, km);
 }
 
 
@@ -789,33 +820,6 @@ sc_status read_maxima(Handle* h, const int32_t* coords, int64_t n, int shift, in
 }
 
 }  // namespace
-
-sc_status ensure_group_order(Handle* h, const KMap* km, int tpi) {
-  const int t = tpi - 1;
-  if (t < 0 || t > 1) return set_error(h, SC_EINVAL, "group order: tiles per item must be 1 or 2");
-  if (km->group_order_ready[t]) return SC_OK;
-  const int64_t groups = (km->num_tiles + t) / tpi;
-  if (!km->group_order[t])
-    SC_TRY_CUDA(dev_alloc(h, reinterpret_cast<void**>(&km->group_order[t]),
-                          sizeof(int32_t) * std::max<int64_t>(groups, 1)),
-                "alloc group order");
-  if (groups > 0) {
-    Temps tmp(h);
-    uint32_t* counts;
-    SC_TRY_CUDA(tmp.get(&counts, sizeof(uint32_t) * 2 * kWorkBuckets), "alloc group counts");
-    SC_TRY_CUDA(cudaMemsetAsync(counts, 0, sizeof(uint32_t) * 2 * kWorkBuckets, h->stream), "clear group counts");
-    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((groups + 255) / 256, 4 * h->num_sms));
-    const int64_t split = km->split_tile >= 0 ? km->split_tile : km->num_tiles;
-    ++h->launches;
-    k_group_hist<<<blocks, 256, 0, h->stream>>>(km->tile_mask, km->num_tiles, tpi, groups, split, counts);
-    ++h->launches;
-    k_group_place<<<blocks, 256, 0, h->stream>>>(km->tile_mask, km->num_tiles, tpi, groups, split, counts,
-                                                 counts + kWorkBuckets, km->group_order[t]);
-    SC_TRY_CUDA(cudaGetLastError(), "group order launch");
-  }
-  km->group_order_ready[t] = true;
-  return SC_OK;
-}
 
 sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t out_begin, int64_t n_out, int dilation,
                      uint32_t flags, KMap** out) {
@@ -1114,6 +1118,11 @@ sc_status concat_maps(Handle* h, const KMap* a, const KMap* b, KMap** out) {
   if (e != cudaSuccess) {
     free_kmap(h, km);
     return cuda_error(h, e, "concat maps");
+  }
+  const sc_status st2 = build_group_orders(h, km);
+  if (st2 != SC_OK) {
+    free_kmap(h, km);
+    return st2;
   }
   *out = km;
   return SC_OK;

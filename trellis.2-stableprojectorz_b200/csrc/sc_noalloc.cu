@@ -18,8 +18,11 @@
 //     (different streams or threads at the same time) race on it and must be
 //     ordered by the caller;
 //   * the first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress (with that device current) and caches it; make that
-//     first call before any stream capture on the device.
+//     cudaGetSymbolAddress (with that device current) and caches it;
+//   * every call waits for its own build (it reads the status word back), so
+//     no call can be part of a CUDA graph: a call made while the handle's
+//     stream is being captured is rejected with SC_EINVAL before it enqueues
+//     anything.
 #include "sc_common.cuh"
 #include "sc_internal.h"
 
@@ -76,11 +79,13 @@ __device__ __forceinline__ unsigned long long na_key(int b, int x, int y, int z)
          (static_cast<unsigned long long>(y) << 16) | static_cast<unsigned long long>(z);
 }
 
+// 64-bit finaliser fmix64 of MurmurHash3 (A. Appleby, public domain),
+// folded to 32 bits.
 __device__ __forceinline__ uint32_t na_hash(unsigned long long k) {
-  k ^= k >> 31;
-  k *= 0x7fb5d329728ea185ull;
-  k ^= k >> 27;
-  k *= 0x81dadef4bc2dd44dull;
+  k ^= k >> 33;
+  k *= 0xff51afd7ed558ccdull;
+  k ^= k >> 33;
+  k *= 0xc4ceb9fe1a85ec53ull;
   k ^= k >> 33;
   return static_cast<uint32_t>(k);
 }
@@ -153,9 +158,16 @@ sc_status build_subm_noalloc(Handle* h, const int32_t* coords, int64_t n, int di
     return set_error(h, SC_EINVAL,
                      "sc_kmap_build_noalloc: n exceeds the fixed scratch limit of 131072 voxels; "
                      "use sc_kmap_build for larger inputs");
+  cudaStreamCaptureStatus cap_st = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(h->stream, &cap_st);
+  if (e != cudaSuccess) return cuda_error(h, e, "sc_kmap_build_noalloc: capture query");
+  if (cap_st != cudaStreamCaptureStatusNone)
+    return set_error(h, SC_EINVAL,
+                     "sc_kmap_build_noalloc waits for its build on the handle's stream and cannot be called "
+                     "while that stream is being captured");
   NaSlot* slots = nullptr;
   int* status = nullptr;
-  cudaError_t e = na_setup(h->device, &slots, &status);
+  e = na_setup(h->device, &slots, &status);
   if (e != cudaSuccess) return cuda_error(h, e, "sc_kmap_build_noalloc: cudaGetSymbolAddress");
   if (n == 0) return SC_OK;
   uint32_t cap = 1024;

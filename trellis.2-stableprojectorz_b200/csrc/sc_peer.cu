@@ -29,28 +29,38 @@ __global__ void __launch_bounds__(kPushThreads) k_halo_push(const uint4* __restr
                                                             const int64_t* __restrict__ dst_off, int64_t n_send,
                                                             void* const* peer_bufs, uint32_t* const* peer_flags,
                                                             int world, int rank, uint32_t epoch,
-                                                            unsigned int* ticket) {
+                                                            unsigned int* ticket, int* err) {
   // one 16-byte vector per thread: consecutive threads cover a row, then the next row
   const int64_t total = n_send * row_vecs;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kPushThreads;
   for (int64_t e = blockIdx.x * static_cast<int64_t>(kPushThreads) + threadIdx.x; e < total; e += stride) {
     const int64_t k = e / row_vecs;
     const int c = static_cast<int>(e - k * row_vecs);
+    const int peer = dst_peer[k];
+    const int64_t off = dst_off[k];
+    // a destination outside the other ranks' buffers or not 16-byte aligned
+    // is skipped and reported (SC_EINVAL in the handle's error word)
+    if (peer < 0 || peer >= world || peer == rank || off < 0 || (off & 15) != 0) {
+      record_error(err, SC_EINVAL);
+      continue;
+    }
     const uint4 val = __ldg(feats + static_cast<int64_t>(src_row[k]) * row_vecs + c);
-    reinterpret_cast<uint4*>(static_cast<uint8_t*>(peer_bufs[dst_peer[k]]) + dst_off[k])[c] = val;
+    reinterpret_cast<uint4*>(static_cast<uint8_t*>(peer_bufs[peer]) + off)[c] = val;
   }
   // The block barrier orders every thread's row stores before thread 0's
   // system-scope fence (fences are cumulative over what the barrier made
-  // visible to thread 0), which orders them before the block's ticket; the
-  // last block to take a ticket publishes the epoch to every peer.  One fence
-  // per block rather than one per thread: each system-scope fence waits for
-  // the stores it orders to be acknowledged.
+  // visible to thread 0), which orders them before the block's ticket.  The
+  // ticket is taken with acquire-release semantics, so the last block's
+  // thread 0 also acquires every earlier block's released stores; the block
+  // barrier then passes them to the threads that publish the epoch to every
+  // peer.  One fence per block rather than one per thread: each system-scope
+  // fence waits for the stores it orders to be acknowledged.
   __syncthreads();
   __shared__ bool last;
   if (threadIdx.x == 0) {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     unsigned int prev;
-    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ticket) : "memory");
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ticket) : "memory");
     last = prev == gridDim.x - 1;
   }
   __syncthreads();
@@ -129,7 +139,7 @@ sc_status halo_push(Handle* h, const void* feats, int row_bytes, const int32_t* 
   ++h->launches;
   k_halo_push<<<blocks, kPushThreads, 0, h->stream>>>(static_cast<const uint4*>(feats), row_bytes / 16, src_row,
                                                       dst_peer, dst_off, n_send, peer_bufs, peer_flags, world, rank,
-                                                      epoch, static_cast<unsigned int*>(h->push_ticket));
+                                                      epoch, static_cast<unsigned int*>(h->push_ticket), h->derr);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SC_OK : cuda_error(h, e, "halo push launch");
 }

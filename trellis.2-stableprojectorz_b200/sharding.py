@@ -32,7 +32,7 @@ import dataclasses
 import torch
 
 __all__ = ["morton_codes", "MortonPartition", "HaloPlan", "build_halo_plan", "exchange_halo", "local_coords",
-           "owned_local", "peer_destinations", "PeerHaloExchange"]
+           "owned_local", "peer_destinations", "PeerHaloExchange", "lpt_assign", "batch_rows"]
 
 _OFFS26 = [(dx, dy, dz) for dx in (-1, 0, 1) for dy in (-1, 0, 1) for dz in (-1, 0, 1) if (dx, dy, dz) != (0, 0, 0)]
 
@@ -74,6 +74,25 @@ class MortonPartition:
     def owner(self, codes):
         return torch.searchsorted(self.bounds, codes, right=True) - 1
 
+    def coarsen(self):
+        """The same ranges one level down (codes of parents ``(b, x>>1, y>>1, z>>1)``).
+
+        A parent's code is its children's code shifted right by 3 (the batch
+        field shifts with them, so it is re-aligned).  With boundaries that
+        are multiples of 8, every 2x2x2 sibling group is owned by one rank, so
+        every parent is owned by the rank that owns its children and the
+        stride-2 down / up convs need no exchange.
+        """
+        lo, hi = torch.iinfo(torch.int64).min, torch.iinfo(torch.int64).max
+        out = []
+        for v in self.bounds.tolist():
+            if v in (lo, hi):
+                out.append(v)
+                continue
+            b, m = v >> 48, v & ((1 << 48) - 1)
+            out.append((b << 48) | (m >> 3))
+        return MortonPartition(torch.tensor(out, dtype=torch.int64, device=self.bounds.device))
+
     def owned_rows(self, coords, rank):
         """Rows of a (global) coord array owned by `rank`, in input order."""
         return torch.nonzero(self.owner(morton_codes(coords)) == rank).squeeze(1)
@@ -96,8 +115,13 @@ class HaloPlan:
         return int(self.halo_coords.shape[0])
 
 
-def build_halo_plan(owned_coords, partition, rank, world, group=None):
-    """Collective: every rank calls it with its owned coords (int32 (n, 4))."""
+def build_halo_plan(owned_coords, partition, rank, world, group=None, interior_first=True):
+    """Collective: every rank calls it with its owned coords (int32 (n, 4)).
+
+    With ``interior_first`` (default) the local order puts rows that read no
+    halo row first (for convs that overlap the exchange); without it the
+    local order is the caller's order (``order`` is the identity), so a
+    tensor over the owned rows can be used as the local rows directly."""
     import torch.distributed as dist
     dev = owned_coords.device
     c = owned_coords.to(torch.int64)
@@ -111,8 +135,12 @@ def build_halo_plan(owned_coords, partition, rank, world, group=None):
         need[own, torch.arange(n, device=dev)] = True
     need[rank] = False
     boundary = need.any(0)
-    order = torch.cat([torch.nonzero(~boundary).squeeze(1), torch.nonzero(boundary).squeeze(1)])
-    n_interior = int(n - int(boundary.sum()))
+    if interior_first:
+        order = torch.cat([torch.nonzero(~boundary).squeeze(1), torch.nonzero(boundary).squeeze(1)])
+        n_interior = int(n - int(boundary.sum()))
+    else:
+        order = torch.arange(n, device=dev)
+        n_interior = 0
     local_of = torch.empty_like(order)
     local_of[order] = torch.arange(n, device=dev)
     idx, splits = [], []
@@ -263,6 +291,12 @@ class PeerHaloExchange:
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
 
+    def next_owned_rows(self):
+        """Owned rows (n_own, C) of the region the next ``exchange()`` / ``push()``
+        sends from: a layer that produces this rank's features writes them
+        here, and the exchange then fills the same region's halo rows."""
+        return self.region_view((self.epoch + 1) & 1)[:self.plan.n_own]
+
     def region_view(self, parity):
         """Local features of region `parity`: (n_own + n_halo, C), owned rows first."""
         arr = _DeviceArray(self.base + parity * self.region, (self.n_rows, self.channels), _TYPESTR[self.dtype])
@@ -320,3 +354,28 @@ class PeerHaloExchange:
         if self.base:
             self.lib.sc_peer_free(self.engine.handle, self.base)
             self.base = 0
+
+
+def lpt_assign(sizes, world):
+    """Greedy longest-processing-time assignment of independent items (batch
+    elements of differing voxel counts) to ``world`` ranks: items in
+    descending size order, each to the rank with the least total so far (ties
+    to the lower rank).  Returns one sorted list of item indices per rank; the
+    same on every rank (a pure function of ``sizes``)."""
+    order = sorted(range(len(sizes)), key=lambda i: (-int(sizes[i]), i))
+    load = [0] * world
+    out = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda k: (load[k], k))
+        out[r].append(i)
+        load[r] += int(sizes[i])
+    return [sorted(x) for x in out]
+
+
+def batch_rows(coords, batches):
+    """Rows of ``coords`` whose batch index is in ``batches``, in input order."""
+    b = coords[:, 0].to(torch.int64)
+    keep = torch.zeros_like(b, dtype=torch.bool)
+    for v in batches:
+        keep |= b == int(v)
+    return torch.nonzero(keep).squeeze(1)
