@@ -31,8 +31,11 @@ Functions and the reference lines they follow:
 * ``conv_gather`` -- pass 2's sum ``out[n,co] = b[co] + sum_v sum_ci
   f[map[n,v],ci] * W[co,v,ci]`` (``src/sparse/ops/conv3d_wgsl.ts:177-222``)
   with weight layout ``(Co,Kd,Kh,Kw,Ci)`` (``src/sparse/ops/conv3d.ts:5,48-49``),
-  accumulated in float64 (the pass-2 defects listed in ``DESIGN.md`` are not
-  reproduced).
+  accumulated in float64.  The defects of that WGSL pass are not reproduced:
+  its weight tile reads row ``tile + 2*local_co`` instead of
+  ``tile + local_co`` (``conv3d_wgsl.ts:188-197,219``), it returns before a
+  ``workgroupBarrier`` (``:174``), and it accumulates in f16 for f16 inputs
+  (``:177``).
 * ``down2_map`` / ``up2_map`` -- stride-2 2x2x2 down-sample and its transpose
   onto the fine coords; the reference's Python versions are absent, so the
   semantics are the ones fixed by the engine's contract (unique parents in
@@ -44,7 +47,7 @@ import numpy as np
 
 __all__ = [
     "flat_keys", "kmap_bruteforce", "kmap_sorted", "conv_gather", "down2_map",
-    "up2_map", "layer_norm", "silu", "resblock", "offsets27", "dense_conv3d_check",
+    "up2_map", "layer_norm", "silu", "resblock", "round_bf16", "offsets27", "dense_conv3d_check",
     "torch_cpu_kmap", "torch_cpu_conv",
 ]
 
@@ -53,12 +56,15 @@ def offsets27(dilation=1):
     """Offset table for a 3x3x3 kernel, ``v = kd*9 + kh*3 + kw``.
 
     Follows ``kernel_offset`` in ``src/sparse/ops/conv3d_wgsl.ts:91-101``:
-    ``(kd - Kd/2) * dil`` on x, ``(kh - Kh/2) * dil`` on y, ``(kw - Kw/2) * dil`` on z.
+    ``(kd - Kd/2) * dilD`` on x, ``(kh - Kh/2) * dilH`` on y, ``(kw - Kw/2) * dilW``
+    on z.  ``dilation`` is one int or ``(dilD, dilH, dilW)``
+    (``src/sparse/ops/conv3d.ts:43-45``).
     """
+    dd, dh, dw = (dilation,) * 3 if np.isscalar(dilation) else tuple(int(d) for d in dilation)
     out = np.zeros((27, 3), np.int64)
     for v in range(27):
         kd, kh, kw = v // 9, (v // 3) % 3, v % 3
-        out[v] = ((kd - 1) * dilation, (kh - 1) * dilation, (kw - 1) * dilation)
+        out[v] = ((kd - 1) * dd, (kh - 1) * dh, (kw - 1) * dw)
     return out
 
 
@@ -99,8 +105,12 @@ def kmap_bruteforce(coords, spatial_shape, batch_size, dilation=1):
     return out
 
 
-def kmap_sorted(coords, spatial_shape, dilation=1):
-    """Sort + searchsorted neighbour map ``[N, 27]`` int32 (any size)."""
+def kmap_sorted(coords, spatial_shape, dilation=1, rows=None):
+    """Sort + searchsorted neighbour map ``[N, 27]`` int32 (any size).
+
+    ``rows`` (optional index array) restricts the output to those map rows,
+    ``[len(rows), 27]``; neighbours are still looked up among all voxels.
+    ``dilation`` is one int (all axes) or ``(dil_x, dil_y, dil_z)``."""
     c = np.asarray(coords).astype(np.int64)
     X, Y, Z = (int(s) for s in spatial_shape)
     keys = flat_keys(c, spatial_shape)
@@ -109,11 +119,12 @@ def kmap_sorted(coords, spatial_shape, dilation=1):
     if len(sk) > 1 and np.any(sk[1:] == sk[:-1]):
         raise ValueError("duplicate coordinate")
     n = len(c)
-    out = np.full((n, 27), -1, np.int32)
+    q_c = c if rows is None else c[np.asarray(rows)]
+    out = np.full((len(q_c), 27), -1, np.int32)
     for v, (dx, dy, dz) in enumerate(offsets27(dilation)):
-        nx, ny, nz = c[:, 1] + dx, c[:, 2] + dy, c[:, 3] + dz
+        nx, ny, nz = q_c[:, 1] + dx, q_c[:, 2] + dy, q_c[:, 3] + dz
         ok = (nx >= 0) & (nx < X) & (ny >= 0) & (ny < Y) & (nz >= 0) & (nz < Z)
-        q = ((c[:, 0] * X + nx) * Y + ny) * Z + nz
+        q = ((q_c[:, 0] * X + nx) * Y + ny) * Z + nz
         pos = np.searchsorted(sk, q)
         pos_c = np.minimum(pos, max(n - 1, 0))
         hit = ok & (pos < n) & (sk[pos_c] == q) if n else ok
@@ -196,10 +207,26 @@ def silu(x):
     return x / (1.0 + np.exp(-x))
 
 
-def resblock(feats, kmap, w1, b1, w2, b2, eps=1e-6):
-    """conv -> LayerNorm -> SiLU -> conv, plus identity skip (float64)."""
+def round_bf16(x):
+    """Rounds to the nearest bf16 value (ties to even), returned as float64.
+
+    Used where the engine stores an intermediate in bf16 (the ResBlock's
+    hidden activation, the activations between chained convs)."""
+    a = np.ascontiguousarray(np.asarray(x, np.float64).astype(np.float32))
+    u = a.view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return r.astype(np.uint32).view(np.float32).astype(np.float64)
+
+
+def resblock(feats, kmap, w1, b1, w2, b2, eps=1e-6, hidden_bf16=False):
+    """conv -> LayerNorm -> SiLU -> conv, plus identity skip (float64).
+
+    ``hidden_bf16`` rounds the hidden activation to bf16 between the convs,
+    as an engine that stores it in bf16 does."""
     h = conv_gather(feats, kmap, w1, b1)
     h = silu(layer_norm(h, eps))
+    if hidden_bf16:
+        h = round_bf16(h)
     return conv_gather(h, kmap, w2, b2) + np.asarray(feats, np.float64)
 
 

@@ -125,8 +125,9 @@ struct TcShape {
   static constexpr int kBarBytesPlan = 256, kAlignSlack = 1024;
   static constexpr int kStageBudget = 227 * 1024 - kOutBytes - kBarBytesPlan - kAlignSlack;
   static constexpr int kStagesFit = kStageBudget / kStageBytes;
-  static constexpr int kStages = kStagesFit > 12 ? 12 : kStagesFit;
-  static_assert(kStages >= 2, "not enough shared memory for two stages");
+  // an even count, so each of the two producer groups owns half the slots
+  static constexpr int kStages = (kStagesFit > 12 ? 12 : kStagesFit) & ~1;
+  static_assert(kStages >= 4, "not enough shared memory for four stages");
   static constexpr int kAccCols = TPI * BNMAX;  // TMEM columns of one accumulator buffer
   static constexpr uint32_t kTmemCols =
       (2 * kAccCols <= 32) ? 32 : (2 * kAccCols <= 64) ? 64 : (2 * kAccCols <= 128) ? 128 : (2 * kAccCols <= 256) ? 256 : 512;
@@ -275,9 +276,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::kStages; ++s) {
-      // the stage's group leader arrives once; the TMA copies (and the
-      // leader, for the quads it zero-filled) complete the bytes
-      mbar_init(full0 + 8u * s, 1);
+      // every warp of the stage's producer group posts its bytes with one
+      // arrival; its TMA copies complete them
+      mbar_init(full0 + 8u * s, kGroupWarps);
       mbar_init(empty0 + 8u * s, 1);
     }
     mbar_init(tfull0, 1);
@@ -365,22 +366,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp < kProducerWarps) {
     // ------------------------------------------------------------ producers
     // Two groups of four warps (one per SM sub-partition) take alternate
-    // stages: while one group waits for its ring slot and synchronises, the
-    // other issues, so the sub-partitions' TMA issue paths stay busy (one
-    // sub-partition issues a gather4 only every ~80 cycles; the SM's TMA unit
-    // takes one every ~19).  Within a group every stage is split over the
-    // four warps: warp w issues quads [w*QPW, (w+1)*QPW) of the stage's
-    // TPI*32 row quads from its first QPW lanes (one gather4 = four rows of
-    // one K chunk, rows of -1 read as zeros).  Per stage:
-    //   1. the group leader waits for the slot, posts every byte of the stage
-    //      (all quads + the weight tile) and loads the weight tile by TMA;
-    //   2. barrier 1 (OR of failures): all warps agree on an abort;
-    //   3. lanes issue a gather4 for every quad holding at least one row;
-    //      quads with none are zero-filled by the warp with shared stores and
-    //      fenced to the async proxy (21% of the quads on the 256^3 workload);
-    //   4. barrier 2 (count of zero-filled quads);
-    //   5. the leader completes the zero-filled quads' bytes itself and
-    //      arrives (release), so the MMA sees every byte and every zero store.
+    // stages, so group g only ever uses the ring slots of parity g: while one
+    // group waits for its slot and synchronises, the other issues, keeping
+    // the sub-partitions' TMA issue paths busy (one sub-partition issues a
+    // gather4 only every ~80 cycles; the SM's TMA unit takes one every ~19).
+    // Within a group every stage is split over the four warps: warp w owns
+    // quads [w*QPW, (w+1)*QPW) of the stage's TPI*32 row quads, one per lane
+    // (one gather4 = four rows of one K chunk, rows of -1 read as zeros).
+    // Per stage:
+    //   1. the group leader waits for the slot; a barrier reduction (OR of
+    //      failures) then releases the group, so all warps agree on an abort;
+    //   2. a quad with no row whose slot copy already holds zeros (the lane
+    //      remembers what it last wrote there) is skipped; every other quad
+    //      is gathered, an empty one as four rows of -1 (zero-filled by the
+    //      TMA unit, so nothing but TMA ever writes a stage);
+    //   3. each warp posts its gathers' bytes (warp 0 also the weight tile's)
+    //      with one arrive.expect_tx before issuing them.
     // Each warp loads its lanes' gather indices kIdxAhead of its group's
     // stages ahead into a register ring (plain coalesced loads, no staging).
     constexpr int ROWB = KC * 2;           // bytes per gathered row
@@ -392,7 +393,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int quad_lin = gw * QPW + lane;  // this lane's quad (valid for lane < QPW)
     const int my_tile = quad_lin >> 5, my_quad = quad_lin & 31;
     const bool issuer = lane < QPW;
-    const uint32_t stage_tx = static_cast<uint32_t>(TPI * S::kABytes + bn * KC * 2);
+    const uint32_t b_tx = static_cast<uint32_t>(bn * KC * 2);
     auto load_idx = [&](const Cursor& c) -> int4 {
       const int64_t t = c.g * TPI + my_tile;
       return issuer && t < p.num_tiles
@@ -416,6 +417,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     int64_t sidx = grp;  // position of `cur` in the CTA's stage sequence
     uint32_t used = 0, used_par = 0;  // leader: slots with a stage issued, parity of the last issue
+    uint32_t zero_held = 0;           // slots whose copy of this lane's quad holds zeros
     bool abort = false;
     bool waited = !WAIT;  // WAIT: the launch waits for a halo exchange (p.wait_flags)
     while (cur.item >= 0 && !abort) {
@@ -435,8 +437,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (leader) {
           fail = !mbar_wait(empty0 + 8u * stage, phase ^ 1u, p.err);
           if (!fail) {
-            mbar_expect_tx(fb, stage_tx);
-            tma_load_2d(sbase + TPI * S::kABytes, &tmB, cur.v * p.ci + cur.kc * KC, cur.cb * bn, fb);
             used |= 1u << stage;
             used_par = (used_par & ~(1u << stage)) | (phase << stage);
           }
@@ -446,24 +446,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         }
         const int4 r4 = ring[d];
-        const bool empty_quad = issuer && (r4.x & r4.y & r4.z & r4.w) == -1;
-        const uint32_t qdst = sbase + my_tile * S::kABytes + my_quad * QB;
-        if (issuer && !empty_quad) tma_gather4(qdst, &tmF, cur.kc * KC, r4.x, r4.y, r4.z, r4.w, fb);
-        uint32_t zmask = __ballot_sync(0xffffffffu, empty_quad);
-        const bool any_zero = zmask != 0u;
-        while (zmask) {  // the warp zero-fills each empty quad: 16 bytes per lane
-          const int q = __ffs(zmask) - 1;
-          zmask &= zmask - 1u;
-          const uint32_t zdst = __shfl_sync(0xffffffffu, qdst, q);
-          if (lane * 16 < QB)
-            asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(zdst + lane * 16u), "r"(0u) : "memory");
+        const bool empty_quad = (r4.x & r4.y & r4.z & r4.w) == -1;
+        const bool issue = issuer && !(empty_quad && ((zero_held >> stage) & 1u));
+        if (issuer) zero_held = empty_quad ? (zero_held | (1u << stage)) : (zero_held & ~(1u << stage));
+        const uint32_t n_issue = static_cast<uint32_t>(__popc(__ballot_sync(0xffffffffu, issue)));
+        if (lane == 0) {
+          mbar_arrive_expect_tx(fb, n_issue * QB + (gw == 0 ? b_tx : 0u));
+          if (gw == 0) tma_load_2d(sbase + TPI * S::kABytes, &tmB, cur.v * p.ci + cur.kc * KC, cur.cb * bn, fb);
         }
-        if (any_zero) fence_proxy_async_smem();
-        const uint32_t nzero = named_bar_red_popc(bar_id, kGroupWarps * 32, empty_quad);
-        if (leader) {
-          if (nzero) mbar_complete_tx(fb, nzero * QB);
-          mbar_arrive(fb);
-        }
+        __syncwarp();  // the warp's bytes are posted before any of its gathers completes
+        if (issue)
+          tma_gather4(sbase + my_tile * S::kABytes + my_quad * QB, &tmF, cur.kc * KC, r4.x, r4.y, r4.z, r4.w, fb);
         if (ahead.item >= 0) {
           ring[d] = load_idx(ahead);
           step(ahead);
