@@ -148,6 +148,15 @@ SC_API sc_status sc_kmap_build_range(sc_handle* h, const int32_t* coords, int64_
                                      int64_t out_end, int32_t kernel_size, int32_t dilation, uint32_t flags,
                                      sc_kmap** out);
 
+/* As sc_kmap_build_range with a dilation per axis: offset v = kd*9 + kh*3 + kw
+ * is ((kd-1)*dil_x, (kh-1)*dil_y, (kw-1)*dil_z), i.e. the reference's
+ * (dilD, dilH, dilW) with kd on x, kh on y, kw on z
+ * (src/sparse/ops/conv3d.ts:22,43-45; conv3d_wgsl.ts:91-101,115-117).  Each
+ * dilation in [1, 1024].  Replaces the same passes as sc_kmap_build. */
+SC_API sc_status sc_kmap_build_dilated(sc_handle* h, const int32_t* coords, int64_t n_in, int64_t out_begin,
+                                       int64_t out_end, int32_t dil_x, int32_t dil_y, int32_t dil_z, uint32_t flags,
+                                       sc_kmap** out);
+
 /* Stride-2 2x2x2 down-sample map: parents are the unique (b, x>>1, y>>1, z>>1)
  * in ascending lexicographic order; map column = (x&1)*4 + (y&1)*2 + (z&1).
  * Replaces the stride-2 sparse conv of trellis2/modules/sparse/conv (absent

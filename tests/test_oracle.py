@@ -46,6 +46,20 @@ def test_dilated_map(pkg, oracle):
     for d in (2, 3):
         assert np.array_equal(oracle.kmap_bruteforce(w.coords, w.spatial_shape, 1, d),
                               oracle.kmap_sorted(w.coords, w.spatial_shape, d))
+    # per-axis dilation (dilD on x, dilH on y, dilW on z) and map-row subsets
+    for d in ((1, 2, 3), (3, 1, 2)):
+        full = oracle.kmap_bruteforce(w.coords, w.spatial_shape, 1, d)
+        assert np.array_equal(full, oracle.kmap_sorted(w.coords, w.spatial_shape, d))
+        rows = np.random.default_rng(1).choice(w.n, 500, replace=False)
+        assert np.array_equal(full[rows], oracle.kmap_sorted(w.coords, w.spatial_shape, d, rows=rows))
+    off = oracle.offsets27((1, 2, 3))
+    assert off[0].tolist() == [-1, -2, -3] and off[26].tolist() == [1, 2, 3] and off[13].tolist() == [0, 0, 0]
+
+
+def test_round_bf16_matches_torch(oracle):
+    x = np.random.default_rng(2).standard_normal(50000) * 37.0
+    ref = torch.from_numpy(x).float().to(torch.bfloat16).double().numpy()
+    assert np.array_equal(oracle.round_bf16(x), ref)
 
 
 def test_duplicates_rejected(pkg, oracle):

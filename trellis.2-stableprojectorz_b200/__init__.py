@@ -16,5 +16,6 @@ from .sparse_conv import (
 )
 from .host_pipeline import HostConvPipeline
 from . import workloads
+from . import conv_b200
 
 __version__ = "0.1.0"

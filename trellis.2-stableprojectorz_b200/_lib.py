@@ -79,6 +79,7 @@ _SIGNATURES = {
     "sc_kmap_build": (_I32, [_P, _P, _I64, _I32, _I32, _U32, _PP]),
     "sc_kmap_build_ex": (_I32, [_P, _P, _I64, _I64, _I32, _I32, _U32, _PP]),
     "sc_kmap_build_range": (_I32, [_P, _P, _I64, _I64, _I64, _I32, _I32, _U32, _PP]),
+    "sc_kmap_build_dilated": (_I32, [_P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _U32, _PP]),
     "sc_kmap_build_down2": (_I32, [_P, _P, _I64, _U32, _PP]),
     "sc_kmap_build_up2": (_I32, [_P, _P, _U32, _PP]),
     "sc_kmap_build_noalloc": (_I32, [_P, _P, _I64, _I32, _P]),

@@ -268,13 +268,14 @@ sc_status sc_kmap_build(sc_handle* h, const int32_t* coords, int64_t n, int32_t 
   if (dilation < 1 || dilation > 1024) return sc::set_error(H, SC_EINVAL, "dilation must be in [1, 1024]");
   sc::DeviceGuard g(H->device);
   KMap* km = nullptr;
-  const sc_status st = sc::build_subm(H, coords, n, 0, n, dilation, flags, &km);
+  const sc_status st = sc::build_subm(H, coords, n, 0, n, sc::Dil{dilation, dilation, dilation}, flags, &km);
   if (st != SC_OK) return st;
   return wrap_kmap(H, km, flags, out);
 }
 
-sc_status sc_kmap_build_range(sc_handle* h, const int32_t* coords, int64_t n_in, int64_t out_begin, int64_t out_end,
-                              int32_t kernel_size, int32_t dilation, uint32_t flags, sc_kmap** out) {
+sc_status sc_kmap_build_dilated(sc_handle* h, const int32_t* coords, int64_t n_in, int64_t out_begin,
+                                int64_t out_end, int32_t dil_x, int32_t dil_y, int32_t dil_z, uint32_t flags,
+                                sc_kmap** out) {
   if (!h || !out) return SC_EINVAL;
   *out = nullptr;
   Handle* H = &h->impl;
@@ -283,13 +284,22 @@ sc_status sc_kmap_build_range(sc_handle* h, const int32_t* coords, int64_t n_in,
     return sc::set_error(H, SC_EINVAL, "need 0 <= out_begin <= out_end <= n_in");
   if (n_in > 0 && (!coords || !sc::aligned(coords, 16)))
     return sc::set_error(H, SC_EINVAL, "coords must be a 16-byte aligned device pointer");
-  if (kernel_size != 3) return sc::set_error(H, SC_EUNSUPPORTED, "only 3x3x3 submanifold kernels");
-  if (dilation < 1 || dilation > 1024) return sc::set_error(H, SC_EINVAL, "dilation must be in [1, 1024]");
+  for (const int32_t d : {dil_x, dil_y, dil_z})
+    if (d < 1 || d > 1024) return sc::set_error(H, SC_EINVAL, "every dilation must be in [1, 1024]");
   sc::DeviceGuard g(H->device);
   KMap* km = nullptr;
-  const sc_status st = sc::build_subm(H, coords, n_in, out_begin, out_end - out_begin, dilation, flags, &km);
+  const sc_status st =
+      sc::build_subm(H, coords, n_in, out_begin, out_end - out_begin, sc::Dil{dil_x, dil_y, dil_z}, flags, &km);
   if (st != SC_OK) return st;
   return wrap_kmap(H, km, flags, out);
+}
+
+sc_status sc_kmap_build_range(sc_handle* h, const int32_t* coords, int64_t n_in, int64_t out_begin, int64_t out_end,
+                              int32_t kernel_size, int32_t dilation, uint32_t flags, sc_kmap** out) {
+  if (!h || !out) return SC_EINVAL;
+  *out = nullptr;
+  if (kernel_size != 3) return sc::set_error(&h->impl, SC_EUNSUPPORTED, "only 3x3x3 submanifold kernels");
+  return sc_kmap_build_dilated(h, coords, n_in, out_begin, out_end, dilation, dilation, dilation, flags, out);
 }
 
 sc_status sc_kmap_build_ex(sc_handle* h, const int32_t* coords, int64_t n_in, int64_t n_out, int32_t kernel_size,

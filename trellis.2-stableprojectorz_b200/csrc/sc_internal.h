@@ -73,8 +73,13 @@ struct KMap {
 cudaError_t dev_alloc(Handle* h, void** p, size_t bytes);
 void dev_free(Handle* h, void* p);
 
+// Per-axis dilation of a 3x3x3 kernel (dilD on x, dilH on y, dilW on z).
+struct Dil {
+  int x, y, z;
+};
+
 // kmap construction (sc_kmap.cu)
-sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t out_begin, int64_t n_out, int dilation,
+sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t out_begin, int64_t n_out, Dil dilation,
                      uint32_t flags, KMap** out);
 sc_status build_down2(Handle* h, const int32_t* coords, int64_t n, uint32_t flags, KMap** out);
 sc_status build_up2(Handle* h, const KMap* down, uint32_t flags, KMap** out);
@@ -114,9 +119,13 @@ size_t radix_sort_temp_bytes(int64_t n, int key_bytes, int passes);
 sc_status radix_sort_pairs_u64(Handle* h, uint64_t* keys, uint32_t* vals, uint64_t* keys_alt, uint32_t* vals_alt,
                                int64_t n, int begin_bit, int end_bit, void* temp, size_t temp_bytes, int* err,
                                bool* result_in_alt);
+// With hist_ready the caller has zeroed `temp` (radix_sort_temp_bytes) and
+// added every key's digit counts into its first passes x kRadixBins words
+// (pass p counts bits [begin_bit + 8p, begin_bit + 8p + 8)).
+constexpr int kRadixBins = 256;
 sc_status radix_sort_pairs_u32(Handle* h, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,
                                int64_t n, int begin_bit, int end_bit, void* temp, size_t temp_bytes, int* err,
-                               bool* result_in_alt);
+                               bool* result_in_alt, bool hist_ready = false);
 
 sc_status set_error(Handle* h, sc_status st, const std::string& msg);
 sc_status cuda_error(Handle* h, cudaError_t e, const char* what);

@@ -81,10 +81,12 @@ __device__ __forceinline__ bool coord_ok(int4 c) {
          static_cast<unsigned>(c.z) <= 65535u && static_cast<unsigned>(c.w) <= 65535u;
 }
 
-__device__ __forceinline__ void offset27(int v, int dil, int& dx, int& dy, int& dz) {
-  dx = (v / 9 - 1) * dil;
-  dy = ((v / 3) % 3 - 1) * dil;
-  dz = (v % 3 - 1) * dil;
+// Offset v = kd*9 + kh*3 + kw of a 3x3x3 kernel with per-axis dilation: kd
+// on x, kh on y, kw on z (src/sparse/ops/conv3d_wgsl.ts:91-101,115-117).
+__device__ __forceinline__ void offset27(int v, Dil d, int& dx, int& dy, int& dz) {
+  dx = (v / 9 - 1) * d.x;
+  dy = ((v / 3) % 3 - 1) * d.y;
+  dz = (v % 3 - 1) * d.z;
 }
 
 // Tile rows of a concatenated map: the first map's slots, then the second
@@ -116,8 +118,16 @@ __global__ void k_iota(uint32_t* v, int64_t n) {
   if (i < n) v[i] = static_cast<uint32_t>(i);
 }
 
-__global__ void k_hash_insert(const int4* __restrict__ coords, int64_t n, Slot* slots, uint32_t cap_mask, int* err) {
+// Inserts every voxel's key; the same threads also fill the map with -1 and
+// zero the row masks that the half-neighbourhood probe completes afterwards.
+__global__ void k_hash_insert(const int4* __restrict__ coords, int64_t n, Slot* slots, uint32_t cap_mask, int* err,
+                              int32_t* __restrict__ map, int64_t map_ints, uint32_t* __restrict__ row_mask,
+                              int64_t n_out) {
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t e = i; e < map_ints / 4; e += stride) reinterpret_cast<int4*>(map)[e] = make_int4(-1, -1, -1, -1);
+  for (int64_t e = (map_ints / 4) * 4 + i; e < map_ints; e += stride) map[e] = -1;
+  for (int64_t e = i; e < n_out; e += stride) row_mask[e] = 0u;
   if (i >= n) return;
   const int4 c = coords[i];
   if (!coord_ok(c)) {
@@ -165,85 +175,103 @@ __device__ __noinline__ int probe_chain(const ulonglong2* __restrict__ sl, unsig
   return -1;
 }
 
-// One thread per output voxel.  Home slots of all 26 neighbours come from
-// per-axis hash terms computed once; the 13 home-slot loads of a group are
+// Half-neighbourhood probe, one thread per INPUT row a (all n rows): it looks
+// up only the 13 offsets v = 0..12 (the mirror of offset v is 26 - v) and,
+// when a's neighbour at v is row b,
+//   * if a is an output row: map[a - out_lo][v] = b;
+//   * if b is an output row: map[b - out_lo][26 - v] = a.
+// Neighbourhood is symmetric (b is a's neighbour at v exactly when a is b's
+// at 26 - v), so the two writes fill every entry of every output row with
+// half the probes of a full lookup; entries no pair reaches keep the -1 the
+// map was filled with, and each entry is written by exactly one thread.  Row
+// masks collect both kinds of bits with atomicOr (zeroed first).  Home slots
+// come from per-axis hash terms computed once; the 13 home-slot loads are
 // issued together (out-of-range neighbours read a harmless slot and are
 // discarded), and only a home slot holding another key takes the rehash slow
-// path (rare at load <= 1/4).  Neighbour keys are the voxel's packed key plus
-// packed offsets; the row mask is built in registers and each warp's 32 rows
-// are written to the [N,27] map as one contiguous run.
-__global__ void __launch_bounds__(256, 4) k_probe_hash(const int4* __restrict__ coords, int64_t n, int64_t row_base,
-                                                    const Slot* __restrict__ slots, uint32_t cap_mask, int dil,
-                                                    int32_t* __restrict__ map, uint32_t* __restrict__ row_mask,
-                                                    unsigned long long* counters) {
-  // Each warp stages its 32 rows (27 ints each; stride 27 is bank-conflict
-  // free) and writes them as one contiguous run of the [N,27] map.
-  __shared__ int32_t s_rows[8][32 * 27];
+// path (rare at load <= 1/4).  Each warp stages the lower half and centre of
+// its output rows in shared memory and writes them row by row.
+__global__ void __launch_bounds__(256, 4) k_probe_hash(const int4* __restrict__ coords, int64_t n, int64_t out_lo,
+                                                    int64_t out_hi, const Slot* __restrict__ slots, uint32_t cap_mask,
+                                                    int dil_x, int dil_y, int dil_z, int32_t* __restrict__ map,
+                                                    uint32_t* __restrict__ row_mask, unsigned long long* counters) {
+  constexpr int kHalf = 14;  // offsets 0..12 and the centre
+  __shared__ int32_t s_rows[8][32 * kHalf];
   const int lane = threadIdx.x & 31;
-  int32_t* srow = s_rows[threadIdx.x >> 5] + lane * 27;
+  int32_t* srow = s_rows[threadIdx.x >> 5] + lane * kHalf;
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  uint32_t m = 0;
+  const bool is_out = i >= out_lo && i < out_hi;
+  uint32_t own = 0;
+  unsigned cnt = 0;
   if (i < n) {
     const int4 c = coords[i];
     const bool cok = coord_ok(c);
     const unsigned long long base = pack16(c.x, c.y, c.z, c.w);
     const uint32_t hb = axis_term(c.x, kMulB);
-    uint32_t hx[3], hy[3], hz[3], lx[3], ly[3], lz[3];
-    bool vx[3], vy[3], vz[3];
+    uint32_t hx[2], hy[3], hz[3], lx[2], ly[3], lz[3];
+    bool vx[2], vy[3], vz[3];
 #pragma unroll
     for (int a = 0; a < 3; ++a) {
-      const int d = (a - 1) * dil;
-      const int x = c.y + d, y = c.z + d, z = c.w + d;
-      vx[a] = cok && static_cast<unsigned>(x) <= 65535u;
+      const int x = c.y + (a - 1) * dil_x, y = c.z + (a - 1) * dil_y, z = c.w + (a - 1) * dil_z;
+      if (a < 2) {
+        vx[a] = cok && static_cast<unsigned>(x) <= 65535u;
+        hx[a] = axis_term(x >> 2, kMulX);
+        lx[a] = static_cast<uint32_t>(x & 3) << 4;
+      }
       vy[a] = cok && static_cast<unsigned>(y) <= 65535u;
       vz[a] = cok && static_cast<unsigned>(z) <= 65535u;
-      hx[a] = axis_term(x >> 2, kMulX);
       hy[a] = axis_term(y >> 2, kMulY);
       hz[a] = axis_term(z >> 2, kMulZ);
-      lx[a] = static_cast<uint32_t>(x & 3) << 4;
       ly[a] = static_cast<uint32_t>(y & 3) << 2;
       lz[a] = static_cast<uint32_t>(z & 3);
     }
     const ulonglong2* sl = reinterpret_cast<const ulonglong2*>(slots);
+    ulonglong2 sv[13];
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      ulonglong2 sv[13];
+    for (int v = 0; v < 13; ++v) {
+      const int a = v / 9, bb = (v / 3) % 3, cc = v % 3;
+      const uint32_t pos = ((fin32(hb ^ hx[a] ^ hy[bb] ^ hz[cc]) << 6) | lx[a] | ly[bb] | lz[cc]) & cap_mask;
+      sv[v] = __ldg(sl + pos);
+    }
 #pragma unroll
-      for (int k = 0; k < 13; ++k) {
-        const int v = g * 14 + k;  // 0..12, then 14..26
-        const int a = v / 9, bb = (v / 3) % 3, cc = v % 3;
-        const uint32_t pos = ((fin32(hb ^ hx[a] ^ hy[bb] ^ hz[cc]) << 6) | lx[a] | ly[bb] | lz[cc]) & cap_mask;
-        sv[k] = __ldg(sl + pos);
+    for (int v = 0; v < 13; ++v) {
+      const int a = v / 9, bb = (v / 3) % 3, cc = v % 3;
+      const long long dq = (static_cast<long long>((a - 1) * dil_x) << 32) +
+                           (static_cast<long long>((bb - 1) * dil_y) << 16) + static_cast<long long>((cc - 1) * dil_z);
+      const unsigned long long q = base + static_cast<unsigned long long>(dq);
+      int r = -1;
+      if (vx[a] && vy[bb] && vz[cc]) {
+        if (sv[v].x == q) r = static_cast<int>(static_cast<uint32_t>(sv[v].y));
+        else if (sv[v].x != kEmptyKey) r = probe_chain(sl, q, cap_mask);
       }
-#pragma unroll
-      for (int k = 0; k < 13; ++k) {
-        const int v = g * 14 + k;
-        const int a = v / 9, bb = (v / 3) % 3, cc = v % 3;
-        const long long dq = (static_cast<long long>(a - 1) << 32) + (static_cast<long long>(bb - 1) << 16) +
-                             static_cast<long long>(cc - 1);
-        const unsigned long long q = base + static_cast<unsigned long long>(dq * dil);
-        int r = -1;
-        if (vx[a] && vy[bb] && vz[cc]) {
-          if (sv[k].x == q) r = static_cast<int>(static_cast<uint32_t>(sv[k].y));
-          else if (sv[k].x != kEmptyKey) r = probe_chain(sl, q, cap_mask);
+      srow[v] = r;
+      if (r >= 0) {
+        if (is_out) {
+          own |= 1u << v;
+          ++cnt;
         }
-        srow[v] = r;
-        m |= (r >= 0 ? 1u : 0u) << v;
+        if (r >= out_lo && r < out_hi) {
+          map[(static_cast<int64_t>(r) - out_lo) * 27 + (26 - v)] = static_cast<int32_t>(i);
+          atomicOr(&row_mask[r - out_lo], 1u << (26 - v));
+          ++cnt;
+        }
       }
     }
-    srow[13] = static_cast<int>(row_base + i);
-    m |= 1u << 13;
-    row_mask[i] = m;
+    srow[13] = static_cast<int32_t>(i);
+    if (is_out) {
+      own |= 1u << 13;
+      ++cnt;
+      atomicOr(&row_mask[i - out_lo], own);
+    }
   }
   __syncwarp();
   const int64_t first = i - lane;
   if (first < n) {
-    const int rows = static_cast<int>(min(static_cast<int64_t>(32), n - first));
     const int32_t* src = s_rows[threadIdx.x >> 5];
-    int32_t* dst = map + first * 27;
-    for (int e = lane; e < rows * 27; e += 32) dst[e] = src[e];
+    for (int e = lane; e < 32 * kHalf; e += 32) {
+      const int64_t row = first + e / kHalf;
+      if (row >= out_lo && row < out_hi && row < n) map[(row - out_lo) * 27 + e % kHalf] = src[e];
+    }
   }
-  unsigned cnt = __popc(m);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
   if ((threadIdx.x & 31) == 0 && cnt) atomicAdd(&counters[0], static_cast<unsigned long long>(cnt));
@@ -316,7 +344,7 @@ __device__ __forceinline__ int sorted_find(const unsigned long long* __restrict_
 __global__ void __launch_bounds__(128) k_probe_sorted(const int4* __restrict__ coords, int64_t n, int64_t row_base,
                                                       const unsigned long long* __restrict__ skeys,
                                                       const uint32_t* __restrict__ svals, int64_t n_keys,
-                                                      Packing pk, int dil,
+                                                      Packing pk, Dil dil,
                                                       int32_t* __restrict__ map, uint32_t* __restrict__ row_mask,
                                                       unsigned long long* counters) {
   __shared__ int32_t s_map[128 * 27];
@@ -536,17 +564,10 @@ sc_status alloc_kmap(Handle* h, KMap* km) {
 // neighbours (most significant), so rows that share corner/edge patterns sort
 // together.  On the 256^3 shell workload this ordering raises the useful
 // fraction of tile work from 0.72 (mask value order) to 0.75.  2x2x2 maps use
-// the mask itself.
-__global__ void k_sort_keys(const uint32_t* __restrict__ row_mask, int64_t n, int K, uint32_t* __restrict__ keys,
-                            uint32_t* __restrict__ perm) {
-  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (i >= n) return;
-  perm[i] = static_cast<uint32_t>(i);
-  const uint32_t m = row_mask[i];
-  if (K != 27) {
-    keys[i] = m;
-    return;
-  }
+// the mask itself.  Sorting on 16 instead of 24 key bits (two passes instead
+// of three) would drop it to 0.72 (0.84 instead of 0.93 on the 1024^3 shell).
+__device__ __forceinline__ uint32_t tile_sort_key(uint32_t m, int K) {
+  if (K != 27) return m;
   uint32_t k = 0;
   int pos = 0;
 #pragma unroll
@@ -560,7 +581,31 @@ __global__ void k_sort_keys(const uint32_t* __restrict__ row_mask, int64_t n, in
       }
     }
   }
-  keys[i] = k;
+  return k;
+}
+
+// Writes every row's sort key and the identity permutation, and adds the
+// key digits of every radix pass (8 bits from begin_bit each) into the
+// sort's histogram: the sort then starts with its first scatter pass.
+constexpr int kKeyHistPasses = 4;
+__global__ void __launch_bounds__(256) k_sort_keys(const uint32_t* __restrict__ row_mask, int64_t n, int K,
+                                                   int begin_bit, int passes, uint32_t* __restrict__ keys,
+                                                   uint32_t* __restrict__ perm, uint32_t* __restrict__ ghist) {
+  __shared__ uint32_t h[kKeyHistPasses][kRadixBins];
+  for (int e = threadIdx.x; e < kKeyHistPasses * kRadixBins; e += blockDim.x) (&h[0][0])[e] = 0;
+  __syncthreads();
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t k = tile_sort_key(row_mask[i], K);
+    keys[i] = k;
+    perm[i] = static_cast<uint32_t>(i);
+    for (int p = 0; p < passes; ++p) atomicAdd(&h[p][(k >> (begin_bit + 8 * p)) & 0xFFu], 1u);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < passes * kRadixBins; e += blockDim.x) {
+    const uint32_t c = (&h[0][0])[e];
+    if (c) atomicAdd(&ghist[e], c);
+  }
 }
 
 // Work order of tile groups for the conv's scheduler: groups of `tpi`
@@ -761,8 +806,6 @@ sc_status finish_tiles(Handle* h, KMap* km, const int32_t* map, uint32_t* row_ma
     SC_TRY_CUDA(tmp.get(&perm_alt, sizeof(uint32_t) * n), "alloc perm");
     SC_TRY_CUDA(tmp.get(&mask_alt, sizeof(uint32_t) * n), "alloc masks");
     SC_TRY_CUDA(tmp.get(&mask_copy, sizeof(uint32_t) * n), "alloc masks");
-    ++h->launches;
-    k_sort_keys<<<blocks_for(n, 256), 256, 0, h->stream>>>(row_mask, n, km->K, mask_copy, perm);
     // 3x3x3 maps sort on the top 24 of the 26 key bits (three 8-bit passes
     // instead of four): on the 256^3 workload the useful fraction of tile rows
     // goes from 0.754 to 0.752 while one sort pass (~13 us) disappears.
@@ -772,9 +815,14 @@ sc_status finish_tiles(Handle* h, KMap* km, const int32_t* map, uint32_t* row_ma
     const size_t tb = radix_sort_temp_bytes(n, 4, passes);
     void* temp;
     SC_TRY_CUDA(tmp.get(&temp, tb), "alloc sort temp");
+    SC_TRY_CUDA(cudaMemsetAsync(temp, 0, tb, h->stream), "clear sort temp");
+    ++h->launches;
+    const unsigned kgrid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 4 * h->num_sms));
+    k_sort_keys<<<kgrid, 256, 0, h->stream>>>(row_mask, n, km->K, begin_bit, passes, mask_copy, perm,
+                                              static_cast<uint32_t*>(temp));
     bool in_alt = false;
     sc_status st = radix_sort_pairs_u32(h, mask_copy, perm, mask_alt, perm_alt, n, begin_bit, end_bit, temp, tb,
-                                        km->err, &in_alt);
+                                        km->err, &in_alt, /*hist_ready=*/true);
     if (st != SC_OK) return st;
     order = in_alt ? perm_alt : perm;
   }
@@ -821,7 +869,7 @@ sc_status read_maxima(Handle* h, const int32_t* coords, int64_t n, int shift, in
 
 }  // namespace
 
-sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t out_begin, int64_t n_out, int dilation,
+sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t out_begin, int64_t n_out, Dil dilation,
                      uint32_t flags, KMap** out) {
   // Neighbours are looked up among all n input rows; output j is input row
   // out_begin + j, for j in [0, n_out).
@@ -892,11 +940,16 @@ sc_status build_subm(Handle* h, const int32_t* coords, int64_t n, int64_t out_be
       free_kmap(h, km);
       return cuda_error(h, e, "alloc hash table");
     }
+    // the half-neighbourhood probe fills the rest of every map row by mirror
+    // writes and ORs mask bits in: the insert sets the map to -1 and the
+    // masks to 0 first
     ++h->launches;
-    k_hash_insert<<<blocks_for(n, 256), 256, 0, h->stream>>>(c4, n, slots, cap - 1, km->err);
+    k_hash_insert<<<blocks_for(n, 256), 256, 0, h->stream>>>(c4, n, slots, cap - 1, km->err, map, n_out * 27,
+                                                              row_mask, n_out);
     ++h->launches;
-    k_probe_hash<<<blocks_for(n_out, 256), 256, 0, h->stream>>>(c4 + out_begin, n_out, out_begin, slots, cap - 1,
-                                                             dilation, map, row_mask, km->counters);
+    k_probe_hash<<<blocks_for(n, 256), 256, 0, h->stream>>>(c4, n, out_begin, out_begin + n_out, slots, cap - 1,
+                                                         dilation.x, dilation.y, dilation.z, map, row_mask,
+                                                         km->counters);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) {

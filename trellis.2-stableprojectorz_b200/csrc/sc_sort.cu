@@ -1,4 +1,8 @@
-// LSD radix sort of (key, uint32 value) pairs, one-sweep style.
+// LSD radix sort of (key, uint32 value) pairs, one-sweep style (the single
+// histogram pass plus one decoupled look-back pass per digit of A. Adinets and
+// D. Merrill, "Onesweep: A Faster Least Significant Digit Radix Sort for GPUs",
+// 2022; the look-back follows D. Merrill and M. Garland, "Single-pass Parallel
+// Prefix Scan with Decoupled Look-back", 2016).
 //
 // One histogram kernel counts the digits of every pass in a single read of
 // the keys; each pass is then ONE kernel that ranks a 2048-key tile in shared
@@ -182,7 +186,8 @@ __global__ void __launch_bounds__(kRsThreads) rs_onesweep_kernel(const K* __rest
 
 template <typename K>
 sc_status radix_sort_impl(Handle* h, K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt, int64_t n,
-                          int begin_bit, int end_bit, void* temp, size_t temp_bytes, int* err, bool* in_alt) {
+                          int begin_bit, int end_bit, void* temp, size_t temp_bytes, int* err, bool* in_alt,
+                          bool hist_ready) {
   *in_alt = false;
   const int passes = (end_bit - begin_bit + 7) / 8;
   if (n <= 0 || passes <= 0) return SC_OK;
@@ -194,11 +199,14 @@ sc_status radix_sort_impl(Handle* h, K* keys, uint32_t* vals, K* keys_alt, uint3
   uint32_t* ghist = static_cast<uint32_t*>(temp);
   uint32_t* counters = ghist + passes * kRsBins;
   uint32_t* status = counters + 64;
-  cudaError_t e = cudaMemsetAsync(temp, 0, need, h->stream);
-  if (e != cudaSuccess) return cuda_error(h, e, "radix sort memset");
-  const int hgrid = static_cast<int>(std::min<int64_t>(ntiles, static_cast<int64_t>(h->num_sms) * 4));
-  ++h->launches;
-  rs_hist_kernel<K><<<hgrid, kRsThreads, 0, h->stream>>>(keys, n, begin_bit, end_bit, passes, ghist);
+  cudaError_t e = cudaSuccess;
+  if (!hist_ready) {
+    e = cudaMemsetAsync(temp, 0, need, h->stream);
+    if (e != cudaSuccess) return cuda_error(h, e, "radix sort memset");
+    const int hgrid = static_cast<int>(std::min<int64_t>(ntiles, static_cast<int64_t>(h->num_sms) * 4));
+    ++h->launches;
+    rs_hist_kernel<K><<<hgrid, kRsThreads, 0, h->stream>>>(keys, n, begin_bit, end_bit, passes, ghist);
+  }
   K* ksrc = keys;
   K* kdst = keys_alt;
   uint32_t* vsrc = vals;
@@ -230,14 +238,14 @@ sc_status radix_sort_pairs_u64(Handle* h, uint64_t* keys, uint32_t* vals, uint64
                                bool* in_alt) {
   return radix_sort_impl<unsigned long long>(h, reinterpret_cast<unsigned long long*>(keys), vals,
                                              reinterpret_cast<unsigned long long*>(keys_alt), vals_alt, n, begin_bit,
-                                             end_bit, temp, temp_bytes, err, in_alt);
+                                             end_bit, temp, temp_bytes, err, in_alt, false);
 }
 
 sc_status radix_sort_pairs_u32(Handle* h, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,
                                int64_t n, int begin_bit, int end_bit, void* temp, size_t temp_bytes, int* err,
-                               bool* in_alt) {
+                               bool* in_alt, bool hist_ready) {
   return radix_sort_impl<uint32_t>(h, keys, vals, keys_alt, vals_alt, n, begin_bit, end_bit, temp, temp_bytes, err,
-                                   in_alt);
+                                   in_alt, hist_ready);
 }
 
 }  // namespace sc

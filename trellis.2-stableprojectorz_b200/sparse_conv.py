@@ -170,6 +170,9 @@ def _flags(tile_sort, check, halo=False):
 def build_kmap(coords, dilation=1, engine=None, tile_sort=True, check=True, n_out=None, out_begin=0, halo=False):
     """Submanifold 3x3x3 neighbour map (``sc_kmap_build``).
 
+    ``dilation`` is one int or ``(dil_x, dil_y, dil_z)`` -- the reference's
+    ``(dilD, dilH, dilW)``, kd pairing with x (``sc_kmap_build_dilated``).
+
     With ``n_out`` / ``out_begin`` only rows ``[out_begin, out_begin + n_out)``
     are outputs (map row j is input row ``out_begin + j``) while neighbours are
     looked up among all rows (``sc_kmap_build_range``; sharded convs order a
@@ -185,6 +188,17 @@ def build_kmap(coords, dilation=1, engine=None, tile_sort=True, check=True, n_ou
     eng.bind_stream()
     p = ctypes.c_void_p()
     n = coords.shape[0]
+    dil = tuple(int(d) for d in dilation) if hasattr(dilation, "__len__") else (int(dilation),) * 3
+    if len(dil) != 3:
+        raise ValueError("dilation must be an int or (dil_x, dil_y, dil_z)")
+    if len(set(dil)) != 1:
+        begin = int(out_begin)
+        n_out = n - begin if n_out is None else int(n_out)
+        eng.check(eng.lib.sc_kmap_build_dilated(eng.handle, _ptr(coords), n, begin, begin + n_out, dil[0], dil[1],
+                                                dil[2], _flags(tile_sort, check, halo), ctypes.byref(p)),
+                  "sc_kmap_build_dilated")
+        return KernelMap(eng, p, L.SC_KMAP_SUBM, n, n_out, 27)
+    dilation = dil[0]
     if n_out is None and out_begin == 0:
         eng.check(eng.lib.sc_kmap_build(eng.handle, _ptr(coords), n, 3, int(dilation),
                                         _flags(tile_sort, check, halo), ctypes.byref(p)), "sc_kmap_build")
@@ -359,8 +373,6 @@ class SparseConv3d:
         dl = tuple(dilation) if not isinstance(dilation, int) else (dilation,) * 3
         if ks != (3, 3, 3):
             raise NotImplementedError("only 3x3x3 submanifold kernels are implemented")
-        if len(set(dl)) != 1:
-            raise NotImplementedError("anisotropic dilation is not implemented")
         if weight.dim() != 5 or tuple(weight.shape[1:4]) != ks:
             raise ValueError("weight must be (Co, Kd, Kh, Kw, Ci)")
         self.weight = weight
@@ -380,7 +392,7 @@ class SparseConv3d:
     def neighbour_map(self, x):
         km = x.get_spatial_cache(self.cache_key())
         if km is None:
-            km = build_kmap(x.coords, self.dilation[0])
+            km = build_kmap(x.coords, self.dilation)
             x.register_spatial_cache(self.cache_key(), km)
         return km
 
