@@ -1024,7 +1024,7 @@ sc_status launch_tc(Handle* h, const KMap* km, const void* feats, const void* we
   // Work order balances CTAs that run few items (10 per CTA on the 256^3
   // workload: -9% conv time); with many items per CTA static striding is
   // already balanced and the natural tile order keeps better L2 locality.
-  p.group_order = p.num_items < kWorkOrderMaxItemsPerCta * grid ? km->group_order[TPI - 1] : nullptr;
+  p.group_order = p.num_items < kWorkOrderMaxItemsPerCta * grid ? km->group_order[TPI == 4 ? 2 : TPI - 1] : nullptr;
   ++h->launches;
   kern<<<static_cast<unsigned>(grid), kTcThreads, S::kSmemBytes, h->stream>>>(tb, tf, p);
   e = cudaGetLastError();
@@ -1035,6 +1035,12 @@ template <int KC, bool BF16>
 sc_status dispatch_bn(Handle* h, const KMap* km, const void* feats, const void* weight, const TcParams& p) {
   // Up to 128 output channels two tiles share each weight stage; wider
   // outputs already reuse each gathered row across 256 MMA columns.
+  // Up to 64 output channels with K chunks of at most 32 channels, four tiles
+  // share each weight stage: the stages are small and their fixed cost
+  // dominates (1024^3 Ci = Co = 32: 1.51 -> 1.16 ms against two tiles).
+  if constexpr (KC <= 32) {
+    if (p.bn <= 64) return launch_tc<KC, 64, 4, BF16>(h, km, feats, weight, p);
+  }
   if (p.bn <= 64) return launch_tc<KC, 64, 2, BF16>(h, km, feats, weight, p);
   if (p.bn <= 128) return launch_tc<KC, 128, 2, BF16>(h, km, feats, weight, p);
   return launch_tc<KC, 256, 1, BF16>(h, km, feats, weight, p);

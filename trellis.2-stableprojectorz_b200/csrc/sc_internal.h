@@ -46,11 +46,12 @@ struct KMap {
   int32_t* gidx = nullptr;
   int32_t* tile_rows = nullptr;
   uint32_t* tile_mask = nullptr;
-  // Groups of TPI = 1, 2 consecutive tiles ordered by descending work (number
-  // of offsets the group runs); the conv schedules its items in this order.
-  // Built with the map, on its stream, when a conv could use it (fewer than
-  // kWorkOrderMaxItemsPerCta * num_sms groups); null otherwise.
-  int32_t* group_order[2] = {nullptr, nullptr};
+  // Groups of TPI = 1, 2, 4 consecutive tiles (index 0, 1, 2) ordered by
+  // descending work (number of offsets the group runs); the conv schedules
+  // its items in this order.  Built with the map, on its stream, when a conv
+  // could use it (fewer than kWorkOrderMaxItemsPerCta * num_sms groups); null
+  // otherwise.
+  int32_t* group_order[3] = {nullptr, nullptr, nullptr};
   // Halo tiles (SC_BUILD_HALO): tiles are output rows in order; per tile the
   // distinct input rows its gathers read (kHaloCap slots, padded with -1 to a
   // multiple of 4) and per (tile, offset, slot) the position of the gathered

@@ -626,27 +626,30 @@ __device__ __forceinline__ int group_bucket(const uint32_t* tile_mask, int64_t g
   return 32 - __popc(m) + (end > split ? 33 : 0);  // more offsets first, late class last
 }
 
-// Both work orders (groups of one and of two tiles) in one single-CTA
+// The work orders of groups of one, two and four tiles in one single-CTA
 // launch: bucket counts in shared memory, an exclusive scan turns them into
 // placement cursors, and a second pass places every group.  An order is
 // written only where its pointer is non-null.
 constexpr int kOrderThreads = 1024;
+constexpr int kOrders = 3;  // tiles per group 1 << k
 
 __global__ void __launch_bounds__(kOrderThreads) k_group_orders(const uint32_t* __restrict__ tile_mask,
                                                                 int64_t num_tiles, int64_t split, int32_t* order1,
-                                                                int32_t* order2) {
-  __shared__ uint32_t cur[2][kWorkBuckets];
-  for (int b = threadIdx.x; b < 2 * kWorkBuckets; b += blockDim.x) cur[b / kWorkBuckets][b % kWorkBuckets] = 0;
+                                                                int32_t* order2, int32_t* order4) {
+  __shared__ uint32_t cur[kOrders][kWorkBuckets];
+  int32_t* const orders[kOrders] = {order1, order2, order4};
+  for (int b = threadIdx.x; b < kOrders * kWorkBuckets; b += blockDim.x) cur[b / kWorkBuckets][b % kWorkBuckets] = 0;
   __syncthreads();
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    if (!(k ? order2 : order1)) continue;
-    const int64_t groups = (num_tiles + k) / (k + 1);
+  for (int k = 0; k < kOrders; ++k) {
+    if (!orders[k]) continue;
+    const int tpi = 1 << k;
+    const int64_t groups = (num_tiles + tpi - 1) / tpi;
     for (int64_t g = threadIdx.x; g < groups; g += blockDim.x)
-      atomicAdd(&cur[k][group_bucket(tile_mask, g, num_tiles, k + 1, split)], 1u);
+      atomicAdd(&cur[k][group_bucket(tile_mask, g, num_tiles, tpi, split)], 1u);
   }
   __syncthreads();
-  if (threadIdx.x < 2) {
+  if (threadIdx.x < kOrders) {
     uint32_t acc = 0;
     for (int b = 0; b < kWorkBuckets; ++b) {
       const uint32_t c = cur[threadIdx.x][b];
@@ -656,12 +659,13 @@ __global__ void __launch_bounds__(kOrderThreads) k_group_orders(const uint32_t* 
   }
   __syncthreads();
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    int32_t* order = k ? order2 : order1;
+  for (int k = 0; k < kOrders; ++k) {
+    int32_t* order = orders[k];
     if (!order) continue;
-    const int64_t groups = (num_tiles + k) / (k + 1);
+    const int tpi = 1 << k;
+    const int64_t groups = (num_tiles + tpi - 1) / tpi;
     for (int64_t g = threadIdx.x; g < groups; g += blockDim.x)
-      order[atomicAdd(&cur[k][group_bucket(tile_mask, g, num_tiles, k + 1, split)], 1u)] = static_cast<int32_t>(g);
+      order[atomicAdd(&cur[k][group_bucket(tile_mask, g, num_tiles, tpi, split)], 1u)] = static_cast<int32_t>(g);
   }
 }
 
@@ -770,7 +774,8 @@ sc_status build_halo(Handle* h, KMap* km, const int32_t* map) {
   return SC_OK;
 }
 
-// Work orders of the conv's scheduler, built with the map on its stream so
+// Work orders of the conv's scheduler (1, 2 and 4 tiles per item), built with
+// the map on its stream so
 // that whatever is ordered after the build (any stream, any handle) sees
 // them.  A conv uses the order of its tiles-per-item count only when it runs
 // fewer than kWorkOrderMaxItemsPerCta items per CTA, and it runs at least one
@@ -779,16 +784,20 @@ sc_status build_halo(Handle* h, KMap* km, const int32_t* map) {
 sc_status build_group_orders(Handle* h, KMap* km) {
   if (km->num_tiles == 0) return SC_OK;
   const int64_t split = km->split_tile >= 0 ? km->split_tile : km->num_tiles;
-  for (int t = 0; t < 2; ++t) {
-    const int64_t groups = (km->num_tiles + t) / (t + 1);
-    if (groups < kWorkOrderMaxItemsPerCta * h->num_sms)
+  bool any = false;
+  for (int t = 0; t < kOrders; ++t) {
+    const int64_t tpi = int64_t{1} << t;
+    const int64_t groups = (km->num_tiles + tpi - 1) / tpi;
+    if (groups < kWorkOrderMaxItemsPerCta * h->num_sms) {
       SC_TRY_CUDA(dev_alloc(h, reinterpret_cast<void**>(&km->group_order[t]), sizeof(int32_t) * groups),
                   "alloc group order");
+      any = true;
+    }
   }
-  if (!km->group_order[0] && !km->group_order[1]) return SC_OK;
+  if (!any) return SC_OK;
   ++h->launches;
   k_group_orders<<<1, kOrderThreads, 0, h->stream>>>(km->tile_mask, km->num_tiles, split, km->group_order[0],
-                                                      km->group_order[1]);
+                                                      km->group_order[1], km->group_order[2]);
   SC_TRY_CUDA(cudaGetLastError(), "group order launch");
   return SC_OK;
 }
@@ -1123,8 +1132,7 @@ void free_kmap(Handle* h, KMap* km) {
   dev_free(h, km->halo_rows);
   dev_free(h, km->halo_n);
   dev_free(h, km->lidx);
-  dev_free(h, km->group_order[0]);
-  dev_free(h, km->group_order[1]);
+  for (int32_t* o : km->group_order) dev_free(h, o);
   dev_free(h, km->out_coords);
   dev_free(h, km->parent_of);
   dev_free(h, km->counters);
