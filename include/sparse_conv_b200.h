@@ -229,6 +229,33 @@ SC_API sc_status sc_conv3d_down2(sc_handle* h, const sc_kmap* km, const void* fe
 SC_API sc_status sc_conv3d_up2(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight, const void* bias,
                         void* out, int32_t ci, int32_t co, sc_dtype dtype, uint32_t epilogue);
 
+/* Depthwise 3x3x3 submanifold conv: out[n, c] = bias[c] + sum_v W[c, v] *
+ * feats[map[n, v], c], weight (C, 3, 3, 3, 1) with v = kd*9 + kh*3 + kw, f32
+ * accumulation in ascending v.  This is the decoder ConvNeXt block's dw_conv
+ * (src/models/sparse_unet_vae_decoder.ts:48-59,122-132, which runs it through
+ * the dense conv of src/sparse/ops/conv3d.ts:40-75) for a depthwise
+ * checkpoint weight.  `km` must be a 3x3x3 submanifold map; channels a
+ * multiple of 8; feats and out 16-byte aligned device arrays [n_in, C] and
+ * [n_out, C]; bias may be NULL. */
+SC_API sc_status sc_conv3d_depthwise(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight,
+                              const void* bias, void* out, int32_t channels, sc_dtype dtype);
+
+/* 2x2x2 subdivision.  Every voxel (b, x, y, z) of coords [n, 4] becomes the
+ * children (b, 2x+i, 2y+j, 2z+k), child s = i*4 + j*2 + k, written in
+ * (voxel, s) order to out_coords [*, 4]; out_parent (may be NULL) receives the
+ * voxel index of every child.  child_mask (n bytes, may be NULL = all 8)
+ * keeps child s of voxel p when bit s of child_mask[p] is set.  With
+ * out_feats, child rows get a copy of their parent's row of feats (row_bytes
+ * per row, a multiple of 16; needs out_parent).  *n_out receives the number
+ * of children; with out_coords NULL nothing is written (count only).  More
+ * children than capacity rows gives SC_ERANGE with *n_out set.  With a mask
+ * the call synchronizes the handle's stream to read the count.  Coordinates
+ * must be in [0, 2^30).  This is the upsample that the TS decoder replaces by
+ * a doubled spatialShape (src/models/sparse_unet_vae_decoder.ts:155-175). */
+SC_API sc_status sc_subdivide2(sc_handle* h, const int32_t* coords, int64_t n, const uint8_t* child_mask,
+                        const void* feats, int32_t row_bytes, int32_t* out_coords, int32_t* out_parent,
+                        void* out_feats, int64_t capacity, int64_t* n_out);
+
 /* Row LayerNorm (no affine) + optional SiLU, in place on [n, c] features
  * (src/dense/ops/layer_norm.ts:28-60, src/dense/ops/silu.ts:20-31). */
 SC_API sc_status sc_layernorm_silu(sc_handle* h, void* x, int64_t n, int32_t c, sc_dtype dtype, int32_t apply_silu,

@@ -40,6 +40,12 @@ Functions and the reference lines they follow:
   onto the fine coords; the reference's Python versions are absent, so the
   semantics are the ones fixed by the engine's contract (unique parents in
   ascending packed-key order; child slot ``(x&1)*4 + (y&1)*2 + (z&1)``).
+* ``conv_depthwise`` / ``convnext_block`` -- the VAE decoder's ConvNeXt block
+  (``src/models/sparse_unet_vae_decoder.ts:48-77``): conv -> LayerNorm ->
+  Linear -> LayerNorm -> SiLU -> Linear + skip, with a depthwise
+  ``(C,3,3,3,1)`` conv weight as an alternative to the dense one.
+* ``subdivide2`` -- 2x2x2 voxel subdivision with an optional child mask, the
+  upsample the TS decoder leaves out (``sparse_unet_vae_decoder.ts:155-175``).
 """
 from __future__ import annotations
 
@@ -48,7 +54,7 @@ import numpy as np
 __all__ = [
     "flat_keys", "kmap_bruteforce", "kmap_sorted", "conv_gather", "down2_map",
     "up2_map", "layer_norm", "silu", "resblock", "round_bf16", "offsets27", "dense_conv3d_check",
-    "torch_cpu_kmap", "torch_cpu_conv",
+    "torch_cpu_kmap", "torch_cpu_conv", "conv_depthwise", "convnext_block", "subdivide2",
 ]
 
 
@@ -228,6 +234,79 @@ def resblock(feats, kmap, w1, b1, w2, b2, eps=1e-6, hidden_bf16=False):
     if hidden_bf16:
         h = round_bf16(h)
     return conv_gather(h, kmap, w2, b2) + np.asarray(feats, np.float64)
+
+
+def conv_depthwise(feats, kmap, weight, bias=None):
+    """Depthwise conv ``out[n, c] = bias[c] + sum_v W[c, v] * feats[kmap[n, v], c]``.
+
+    ``weight`` is ``(C, 3, 3, 3, 1)`` (or ``(C, 27)``), ``v = kd*9 + kh*3 + kw``
+    as in ``src/sparse/ops/conv3d.ts:48-49``; float64."""
+    f = np.asarray(feats, np.float64)
+    W = np.asarray(weight, np.float64).reshape(f.shape[1], -1)
+    km = np.asarray(kmap)
+    out = np.zeros((km.shape[0], f.shape[1]), np.float64)
+    if bias is not None:
+        out += np.asarray(bias, np.float64)[None, :]
+    for v in range(km.shape[1]):
+        rows = np.where(km[:, v] >= 0)[0]
+        if len(rows):
+            out[rows] += f[km[rows, v]] * W[None, :, v]
+    return out
+
+
+def convnext_block(feats, kmap, dw_weight, dw_bias, l0_weight, l0_bias, l2_weight, l2_bias, eps=1e-6,
+                   round_to_bf16=False):
+    """Sparse ConvNeXt block of the VAE decoder
+    (``src/models/sparse_unet_vae_decoder.ts:48-77``): dw_conv -> LayerNorm ->
+    Linear0 -> LayerNorm -> SiLU -> Linear2, plus identity skip (float64).
+
+    ``dw_weight`` ``(C, 3, 3, 3, C)`` is a full conv, ``(C, 3, 3, 3, 1)`` a
+    depthwise one, None skips the conv.  Linear weights are ``(out, in)``
+    (``torch.nn.Linear``), i.e. ``x @ W.T``.  ``round_to_bf16`` rounds every
+    intermediate the engine stores in bf16 (conv output after LayerNorm, the
+    Linear0 output, the activation after SiLU)."""
+    f = np.asarray(feats, np.float64)
+    rnd = round_bf16 if round_to_bf16 else (lambda a: a)
+    if dw_weight is None:
+        h = f
+    elif np.asarray(dw_weight).shape[-1] == 1 and f.shape[1] != 1:
+        h = rnd(conv_depthwise(f, kmap, dw_weight, dw_bias))
+    else:
+        h = conv_gather(f, kmap, dw_weight, dw_bias)
+    h = rnd(layer_norm(h, eps))
+    h = h @ np.asarray(l0_weight, np.float64).T
+    if l0_bias is not None:
+        h = h + np.asarray(l0_bias, np.float64)[None, :]
+    h = rnd(silu(layer_norm(rnd(h), eps)))
+    h = h @ np.asarray(l2_weight, np.float64).T
+    if l2_bias is not None:
+        h = h + np.asarray(l2_bias, np.float64)[None, :]
+    return h + f
+
+
+def subdivide2(coords, feats, child_mask=None):
+    """2x2x2 subdivision: each voxel ``(b, x, y, z)`` becomes its children
+    ``(b, 2x+i, 2y+j, 2z+k)``, child ``s = i*4 + j*2 + k``, rows in
+    (parent, s) order, each carrying its parent's features.  ``child_mask``
+    (``[N, 8]`` bool) keeps only the marked children.
+
+    The TS decoder only doubles ``spatialShape`` and keeps the coords
+    (``src/models/sparse_unet_vae_decoder.ts:155-175``); the subdividing
+    module it stands in for (TRELLIS ``SparseSubdivide`` / the
+    ``SparseResBlockUpsample3d`` subdivision mask) lives in the ``trellis2``
+    submodule, absent from the tree, and is restated here from its published
+    behaviour."""
+    c = np.asarray(coords, np.int64)
+    n = c.shape[0]
+    s = np.arange(8)
+    off = np.stack([(s >> 2) & 1, (s >> 1) & 1, s & 1], 1)
+    fine = np.empty((n, 8, 4), np.int64)
+    fine[:, :, 0] = c[:, None, 0]
+    fine[:, :, 1:] = 2 * c[:, None, 1:] + off[None]
+    parent = np.repeat(np.arange(n), 8).reshape(n, 8)
+    keep = np.ones((n, 8), bool) if child_mask is None else np.asarray(child_mask, bool).reshape(n, 8)
+    fine, parent = fine[keep], parent[keep]
+    return fine.astype(np.int32), None if feats is None else np.asarray(feats)[parent]
 
 
 def dense_conv3d_check(coords, feats, weight, bias, spatial_shape, batch_size):

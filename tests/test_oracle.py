@@ -160,3 +160,63 @@ def test_workloads_are_deterministic_and_valid(pkg):
         assert len(np.unique(key)) == len(c)
         assert c.min() >= 0 and c[:, 1:].max() < a.spatial_shape[0]
         assert np.all(np.diff(c[:, 0]) >= 0)  # batch-sorted
+
+
+def test_depthwise_oracle_is_dense_conv_with_diagonal_weight(oracle):
+    rng = np.random.default_rng(21)
+    coords = np.unique(rng.integers(0, 12, (300, 3)), axis=0)
+    coords = np.concatenate([np.zeros((len(coords), 1), np.int64), coords], 1).astype(np.int32)
+    km = oracle.kmap_sorted(coords, (12, 12, 12))
+    c = 5
+    f = rng.standard_normal((len(coords), c))
+    wd = rng.standard_normal((c, 3, 3, 3, 1))
+    b = rng.standard_normal(c)
+    dense = np.zeros((c, 27, c))
+    dense[np.arange(c), :, np.arange(c)] = wd.reshape(c, 27)
+    np.testing.assert_allclose(oracle.conv_depthwise(f, km, wd, b), oracle.conv_gather(f, km, dense, b), rtol=1e-12)
+
+
+def test_convnext_block_oracle_matches_torch(oracle):
+    """The block against torch.nn.functional in float64 (dense conv through
+    the dense-grid check, LayerNorm without affine, eps 1e-6)."""
+    import torch
+    import torch.nn.functional as F
+    rng = np.random.default_rng(22)
+    coords = np.unique(rng.integers(0, 10, (250, 3)), axis=0)
+    coords = np.concatenate([np.zeros((len(coords), 1), np.int64), coords], 1).astype(np.int32)
+    c = 6
+    f = rng.standard_normal((len(coords), c))
+    dw = rng.standard_normal((c, 3, 3, 3, c)) / 10
+    db = rng.standard_normal(c)
+    l0, b0 = rng.standard_normal((4 * c, c)), rng.standard_normal(4 * c)
+    l2, b2 = rng.standard_normal((c, 4 * c)), rng.standard_normal(c)
+    km = oracle.kmap_sorted(coords, (10, 10, 10))
+    got = oracle.convnext_block(f, km, dw, db, l0, b0, l2, b2)
+    h = torch.from_numpy(oracle.dense_conv3d_check(coords, f, dw, db, (10, 10, 10), 1))
+    h = F.layer_norm(h, (c,), eps=1e-6)
+    h = F.linear(h, torch.from_numpy(l0), torch.from_numpy(b0))
+    h = F.silu(F.layer_norm(h, (4 * c,), eps=1e-6))
+    h = F.linear(h, torch.from_numpy(l2), torch.from_numpy(b2)) + torch.from_numpy(f)
+    np.testing.assert_allclose(got, h.numpy(), rtol=1e-9, atol=1e-9)
+
+
+def test_subdivide_oracle_properties(oracle):
+    rng = np.random.default_rng(23)
+    coords = np.unique(rng.integers(0, 50, (400, 4)) * np.array([0, 1, 1, 1]) + np.array([1, 0, 0, 0]) *
+                       rng.integers(0, 3, (400, 1)), axis=0).astype(np.int32)
+    f = rng.standard_normal((len(coords), 3))
+    fine, ff = oracle.subdivide2(coords, f)
+    assert fine.shape == (8 * len(coords), 4)
+    assert len(np.unique(fine, axis=0)) == len(fine)
+    parents = np.concatenate([fine[:, :1], fine[:, 1:] >> 1], 1)
+    assert np.array_equal(parents, np.repeat(coords, 8, axis=0))
+    assert np.array_equal(ff, np.repeat(f, 8, axis=0))
+    # down-sampling the children gives the voxels back, each with all 8 slots filled
+    p, dmap = oracle.down2_map(fine)
+    assert np.array_equal(p, coords[np.lexsort(coords.T[::-1])])
+    assert np.all(dmap >= 0)
+    mask = rng.random((len(coords), 8)) < 0.3
+    fm, fmf = oracle.subdivide2(coords, f, mask)
+    assert len(fm) == mask.sum()
+    keep = mask.ravel()
+    assert np.array_equal(fm, fine[keep]) and np.array_equal(fmf, ff[keep])

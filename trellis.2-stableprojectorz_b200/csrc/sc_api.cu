@@ -487,6 +487,49 @@ sc_status sc_conv3d_up2(sc_handle* h, const sc_kmap* km, const void* feats, cons
   return sc_conv3d(h, km, feats, weight, bias, nullptr, out, ci, co, dtype, epilogue, 0.f);
 }
 
+sc_status sc_conv3d_depthwise(sc_handle* h, const sc_kmap* km, const void* feats, const void* weight,
+                              const void* bias, void* out, int32_t channels, sc_dtype dtype) {
+  if (!h || !km) return SC_EINVAL;
+  Handle* H = &h->impl;
+  const KMap* K = km->impl;
+  if (K->kind != SC_KMAP_SUBM || K->K != 27) return sc::set_error(H, SC_EINVAL, "map is not a 3x3x3 submanifold map");
+  if (dtype != SC_F32 && dtype != SC_BF16 && dtype != SC_F16) return sc::set_error(H, SC_EINVAL, "unknown dtype");
+  if (channels <= 0 || channels % 8 != 0)
+    return sc::set_error(H, SC_EINVAL, "depthwise conv needs a positive channel count that is a multiple of 8");
+  if (K->n_out == 0) return SC_OK;
+  if (!weight || !out || (K->n_in > 0 && !feats)) return sc::set_error(H, SC_EINVAL, "null operand");
+  if (!sc::aligned(feats, 16) || !sc::aligned(out, 16))
+    return sc::set_error(H, SC_EINVAL, "feats and out must be 16-byte aligned");
+  sc::DeviceGuard g(H->device);
+  return sc::conv_depthwise(H, K, feats, weight, bias, out, channels, dtype);
+}
+
+sc_status sc_subdivide2(sc_handle* h, const int32_t* coords, int64_t n, const uint8_t* child_mask,
+                        const void* feats, int32_t row_bytes, int32_t* out_coords, int32_t* out_parent,
+                        void* out_feats, int64_t capacity, int64_t* n_out) {
+  if (!h) return SC_EINVAL;
+  Handle* H = &h->impl;
+  if (!n_out) return sc::set_error(H, SC_EINVAL, "null n_out");
+  *n_out = 0;
+  if (n < 0 || n >= (1ll << 28)) return sc::set_error(H, SC_EINVAL, "n must be in [0, 2^28)");
+  if (n > 0 && (!coords || !sc::aligned(coords, 16)))
+    return sc::set_error(H, SC_EINVAL, "coords must be a 16-byte aligned device pointer");
+  if (out_coords && !sc::aligned(out_coords, 16))
+    return sc::set_error(H, SC_EINVAL, "out_coords must be 16-byte aligned");
+  if (out_feats) {
+    if (!out_coords || !out_parent || (n > 0 && !feats))
+      return sc::set_error(H, SC_EINVAL, "copying features needs feats, out_coords and out_parent");
+    if (row_bytes <= 0 || row_bytes % 16 != 0) return sc::set_error(H, SC_EINVAL, "row_bytes must be a multiple of 16");
+    if (!sc::aligned(out_feats, 16) || (feats && !sc::aligned(feats, 16)))
+      return sc::set_error(H, SC_EINVAL, "feats and out_feats must be 16-byte aligned");
+  }
+  if (capacity < 0) return sc::set_error(H, SC_EINVAL, "capacity must be >= 0");
+  if (n == 0) return SC_OK;
+  sc::DeviceGuard g(H->device);
+  return sc::subdivide2(H, coords, n, child_mask, feats, row_bytes, out_coords, out_parent, out_feats, capacity,
+                        n_out);
+}
+
 sc_status sc_layernorm_silu(sc_handle* h, void* x, int64_t n, int32_t c, sc_dtype dtype, int32_t apply_silu,
                             float eps) {
   if (!h) return SC_EINVAL;

@@ -114,6 +114,13 @@ sc_status conv_simt_f32(Handle* h, const KMap* km, const float* feats, const flo
                         const float* residual, float* out, int ci, int co, uint32_t epi, float eps);
 sc_status check_gather_bounds(Handle* h, const KMap* km);
 sc_status layernorm_silu(Handle* h, void* x, int64_t n, int c, sc_dtype dtype, int silu, float eps);
+// 2x2x2 subdivision with an optional child mask (sc_subdiv.cu)
+sc_status subdivide2(Handle* h, const int32_t* coords, int64_t n, const uint8_t* child_mask, const void* feats,
+                     int row_bytes, int32_t* out_coords, int32_t* out_parent, void* out_feats, int64_t capacity,
+                     int64_t* n_out);
+// depthwise 3x3x3 submanifold conv over a subm map (sc_conv_dw.cu)
+sc_status conv_depthwise(Handle* h, const KMap* km, const void* feats, const void* weight, const void* bias,
+                         void* out, int c, sc_dtype dtype);
 
 // radix sort (sc_sort.cu): sorts (key, value) pairs on bits [begin_bit, end_bit)
 size_t radix_sort_temp_bytes(int64_t n, int key_bytes, int passes);

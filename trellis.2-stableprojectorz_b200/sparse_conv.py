@@ -477,3 +477,119 @@ def sparse_resblock(x, w1, b1, w2, b2, eps=1e-6):
     h = conv3d(km, x.feats, w1, b1, silu=True, layernorm=True, eps=eps)
     out = conv3d(km, h, w2, b2, residual=x.feats)
     return x.replace(out)
+
+
+def conv3d_depthwise(kmap, feats, weight, bias=None, out=None):
+    """Depthwise 3x3x3 submanifold conv (``sc_conv3d_depthwise``):
+    ``out[n, c] = bias[c] + sum_v W[c, v] * feats[map[n, v], c]``.
+
+    ``weight`` is ``(C, 3, 3, 3, 1)`` (or ``(C, 27)``); C a multiple of 8."""
+    dt = _DTYPES.get(feats.dtype)
+    if dt is None:
+        raise TypeError(f"unsupported feature dtype {feats.dtype}")
+    if kmap.kind != L.SC_KMAP_SUBM or kmap.kernel_volume != 27:
+        raise ValueError("depthwise conv needs a 3x3x3 submanifold map")
+    c = int(feats.shape[1]) if feats.dim() == 2 else -1
+    if feats.shape != (kmap.n_in, c) or weight.numel() != 27 * c:
+        raise ValueError(f"feats {tuple(feats.shape)} / weight {tuple(weight.shape)} do not match "
+                         f"({kmap.n_in}, C) / (C, 3, 3, 3, 1)")
+    feats = feats.contiguous()
+    weight = weight.to(feats.dtype).contiguous()
+    if bias is not None:
+        bias = bias.to(feats.dtype).contiguous()
+    if out is None:
+        out = torch.empty((kmap.n_out, c), dtype=feats.dtype, device=feats.device)
+    eng = kmap.engine
+    eng.bind_stream()
+    eng.check(eng.lib.sc_conv3d_depthwise(eng.handle, kmap.ptr, _ptr(feats), _ptr(weight), _ptr(bias), _ptr(out),
+                                          c, dt), "sc_conv3d_depthwise")
+    return out
+
+
+def _linear(x, weight, bias, layout):
+    w = weight.to(x.dtype)
+    w = w.t() if layout == "out_in" else w
+    if bias is None:
+        return x @ w
+    return torch.addmm(bias.to(x.dtype), x, w)
+
+
+def sparse_convnext_block(x, dw_weight, dw_bias, l0_weight, l0_bias, l2_weight, l2_bias, eps=1e-6,
+                          linear_layout="out_in"):
+    """The sparse VAE decoder's ConvNeXt block
+    (``src/models/sparse_unet_vae_decoder.ts:48-77``): ``dw_conv`` ->
+    LayerNorm -> Linear0 -> LayerNorm -> SiLU -> Linear2, plus identity skip.
+
+    * ``dw_weight`` ``(C, 3, 3, 3, C)``: a full conv with the LayerNorm fused
+      into its epilogue (``sc_conv3d`` with ``SC_EPI_LAYERNORM``), the way the
+      TS runs it (``src/sparse/ops/conv3d.ts:48``);
+    * ``dw_weight`` ``(C, 3, 3, 3, 1)``: the depthwise conv
+      (``sc_conv3d_depthwise``) followed by the engine's row LayerNorm;
+    * ``dw_weight`` None: LayerNorm of ``x.feats`` (the TS's ``dwConv`` null).
+
+    Both Linears are plain cuBLAS GEMMs (``torch.addmm``); the LayerNorm + SiLU
+    between them is the engine's row kernel.  ``linear_layout`` "out_in"
+    takes ``torch.nn.Linear`` weights ``(out, in)``; "in_out" takes the
+    ``(in, out)`` matrices the TS ``matmul(a, b)`` multiplies by
+    (``src/runtime/ops/matmul.ts:16-26``)."""
+    if linear_layout not in ("out_in", "in_out"):
+        raise ValueError("linear_layout must be 'out_in' or 'in_out'")
+    if not x.feats.is_cuda:
+        raise ValueError("sparse_convnext_block runs on CUDA tensors only")
+    f = x.feats.contiguous()
+    c = int(f.shape[1])
+    if dw_weight is None:
+        h = layernorm_silu(f.clone(), silu=False, eps=eps)
+    else:
+        km = SparseConv3d(dw_weight).neighbour_map(x)
+        if dw_weight.shape[-1] == 1 and c != 1:
+            h = layernorm_silu(conv3d_depthwise(km, f, dw_weight, dw_bias), silu=False, eps=eps)
+        else:
+            h = conv3d(km, f, dw_weight, dw_bias, layernorm=True, eps=eps)
+    h = layernorm_silu(_linear(h, l0_weight, l0_bias, linear_layout).contiguous(), silu=True, eps=eps)
+    out = _linear(h, l2_weight, l2_bias, linear_layout)
+    return x.replace(out.add_(f))
+
+
+def subdivide2(x, child_mask=None):
+    """2x2x2 subdivision of a :class:`SparseTensor` (``sc_subdivide2``).
+
+    Every voxel ``(b, x, y, z)`` becomes ``(b, 2x+i, 2y+j, 2z+k)``, child
+    ``s = i*4 + j*2 + k``, in (voxel, s) order, each with a copy of its
+    voxel's features.  ``child_mask`` keeps only some children: an ``(N, 8)``
+    bool tensor, or ``(N,)`` uint8 with bit s for child s (the subdivision
+    logits of ``SparseResBlockUpsample3d`` thresholded at 0 give it).  The
+    result's scale is halved and its spatial cache is new.  Returns
+    ``(fine, parent)`` with ``parent[j]`` the voxel row of child j."""
+    coords = _coords_arg(x.coords)
+    n = int(coords.shape[0])
+    feats = x.feats.contiguous()
+    eng = get_engine(coords.device)
+    mask = None
+    if child_mask is not None:
+        m = child_mask.to(coords.device)
+        if m.dtype == torch.bool:
+            if m.shape != (n, 8):
+                raise ValueError("a bool child_mask must be (N, 8)")
+            bits = torch.tensor([1, 2, 4, 8, 16, 32, 64, 128], dtype=torch.int32, device=m.device)
+            m = (m.to(torch.int32) * bits).sum(1).to(torch.uint8)
+        elif m.dtype != torch.uint8 or m.shape != (n,):
+            raise ValueError("child_mask must be (N, 8) bool or (N,) uint8")
+        mask = m.contiguous()
+    row_bytes = int(feats.shape[1]) * feats.element_size()
+    if row_bytes % 16 != 0:
+        raise ValueError("feature rows must be a multiple of 16 bytes")
+    eng.bind_stream()
+    cnt = ctypes.c_int64()
+    if mask is None:
+        total = 8 * n
+    else:
+        eng.check(eng.lib.sc_subdivide2(eng.handle, _ptr(coords), n, _ptr(mask), None, 0, None, None, None, 0,
+                                        ctypes.byref(cnt)), "sc_subdivide2")
+        total = int(cnt.value)
+    out_c = torch.empty((total, 4), dtype=torch.int32, device=coords.device)
+    parent = torch.empty(total, dtype=torch.int32, device=coords.device)
+    out_f = torch.empty((total, feats.shape[1]), dtype=feats.dtype, device=feats.device)
+    eng.check(eng.lib.sc_subdivide2(eng.handle, _ptr(coords), n, _ptr(mask), _ptr(feats), row_bytes, _ptr(out_c),
+                                    _ptr(parent), _ptr(out_f), total, ctypes.byref(cnt)), "sc_subdivide2")
+    return SparseTensor(out_f, out_c, None, tuple(s / 2 for s in x.scale)), parent
