@@ -83,10 +83,18 @@ def parse_args():
                          "peers inside its kernel before its first tile (peer-conv-wait) or, on the "
                          "interior+boundary map, before its first boundary tile (peer-interior-first); or NCCL "
                          "all_to_all_single (nccl)")
-    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "table"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "table", "dec"], default="c2",
                     help="c2: BASELINE configs[1] (default); c3: configs[2] ResBlock batch, data-parallel; "
                          "c4: configs[3] down/subm/up, Morton-sharded; c5: configs[4] 1024^3, Morton-sharded; "
-                         "table: every config on one GPU")
+                         "table: every config on one GPU; dec: the decoder rows (ConvNeXt block with a depthwise "
+                         "conv, 2x2x2 subdivision) on configs[1]'s voxels, one GPU")
+    ap.add_argument("--map-mode", choices=["hash", "sort"], default="hash",
+                    help="c2 on one GPU / replicas: kernel-map construction by hash probe (default) or radix sort")
+    ap.add_argument("--halo-map", action="store_true",
+                    help="c2 on one GPU / replicas: build the map with SC_BUILD_HALO (row-order tiles, halo-staged "
+                         "conv)")
+    ap.add_argument("--configs", default="1,2,3,4,5", help="table: which BASELINE configs (1-based, comma list)")
+    ap.add_argument("--dec-channels", type=int, default=64, help="dec: channels of the ConvNeXt block")
     return ap.parse_args()
 
 
@@ -302,7 +310,7 @@ def run_ours(args):
     peaks, peak_src = measured_peaks()
 
     w, coords_np = make_inputs(rank)
-    eng = pkg.get_engine(dev)
+    eng = pkg.get_engine(dev, map_mode=args.map_mode)
     coords = torch.from_numpy(coords_np).to(dev)
     feats = torch.from_numpy(w.feats).to(dev, torch.bfloat16)
     weight = torch.from_numpy(w.weight).to(dev, torch.bfloat16)
@@ -310,7 +318,7 @@ def run_ours(args):
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
     def step():
-        km = pkg.build_kmap(coords, engine=eng, check=False)
+        km = pkg.build_kmap(coords, engine=eng, check=False, halo=args.halo_map)
         pkg.conv3d(km, feats, weight, out=out)
         return km
 
@@ -334,7 +342,7 @@ def run_ours(args):
         for k in range(args.steps):
             flush.zero_()
             ev[k][0].record()
-            km = pkg.build_kmap(coords, engine=eng, check=False)
+            km = pkg.build_kmap(coords, engine=eng, check=False, halo=args.halo_map)
             ev[k][1].record()
             pkg.conv3d(km, feats, weight, out=out)
             ev[k][2].record()
@@ -378,7 +386,7 @@ def run_ours(args):
     h2d = coords_h.numel() * 4 + feats_h.numel() * 2
     d2h = out_h.numel() * 2
     ref_out = out_h.clone()
-    o_chk = pkg.conv3d(pkg.build_kmap(coords, engine=eng), feats, weight)
+    o_chk = pkg.conv3d(pkg.build_kmap(coords, engine=eng, halo=args.halo_map), feats, weight)
     e2e_matches = bool(torch.equal(o_chk.cpu(), ref_out))
 
     c5 = None if args.no_c5 else c5_block(args, pkg, dist, rank, world, dev, eng, peaks, peak_src)
@@ -402,7 +410,9 @@ def run_ours(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded union of 6 ellipsoid shells at 256^3 (BASELINE configs[1]); the same shape "
                 "on every rank",
-        "config": c2_config(w, world, info["num_pairs"], args.replicas),
+        "config": dict(c2_config(w, world, info["num_pairs"], args.replicas),
+                       **({"map_mode": args.map_mode} if args.map_mode != "hash" else {}),
+                       **({"map_layout": "SC_BUILD_HALO"} if args.halo_map else {})),
         "tile_pairs": info["tile_pairs"],
         "map_build_ms": 1e3 * t_map / args.steps, "conv_ms": 1e3 * conv_s,
         "conv_tflops": roof["achieved"], "conv_pct_of_bf16_peak": 100.0 * roof["frac"],
@@ -439,7 +449,7 @@ def run_sharded_c2(args, pkg, dist, rank, world, dev):
     from sparseconv_b200 import sharding as S
     peaks, peak_src = measured_peaks()
     w, coords_np = make_inputs(rank)
-    eng = pkg.get_engine(dev)
+    eng = pkg.get_engine(dev, map_mode=args.map_mode)
     coords = torch.from_numpy(coords_np).to(dev)
     feats = torch.from_numpy(w.feats).to(dev, torch.bfloat16)
     weight = torch.from_numpy(w.weight).to(dev, torch.bfloat16)
@@ -991,6 +1001,167 @@ def run_c4(args):
     return 0
 
 
+def run_dec(args):
+    """The decoder rows on one GPU, on configs[1]'s 406k voxels: one step is a
+    ConvNeXt block (depthwise 3x3x3 conv -> LayerNorm -> Linear C->4C ->
+    LayerNorm + SiLU -> Linear 4C->C + skip, the map cached per coord set as
+    the decoder does) followed by a 2x2x2 subdivision of its output under a
+    seeded child mask (half the children kept).  Device-timed with the L2
+    flushed between steps; the depthwise conv and the subdivision are also
+    timed alone for their rooflines.  Not the driver's headline line."""
+    import numpy as np
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    rank, local_rank, world = dist_env()
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"workload": "dec", "unavailable": "the decoder rows are measured on one GPU"}))
+        return 0
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, peak_src = measured_peaks()
+    eng = pkg.get_engine(dev)
+    w = pkg.workloads.make_workload(2)
+    C = int(args.dec_channels)
+    rng = np.random.default_rng(2024)
+
+    def dW(shape, scale):
+        return torch.from_numpy((scale * rng.standard_normal(shape)).astype(np.float32)).to(dev, torch.bfloat16)
+
+    ws = (dW((C, 3, 3, 3, 1), 1 / np.sqrt(27)), dW(C, 0.1), dW((4 * C, C), 1 / np.sqrt(C)), dW(4 * C, 0.1),
+          dW((C, 4 * C), 1 / np.sqrt(4 * C)), dW(C, 0.1))
+    coords_np = np.ascontiguousarray(w.coords)
+    feats_np = rng.standard_normal((w.n, C)).astype(np.float32)
+    mask_np = (rng.random((w.n, 8)) < 0.5)
+    bits_np = (mask_np * (1 << np.arange(8))).sum(1).astype(np.uint8)
+    coords = torch.from_numpy(coords_np).to(dev)
+    feats = torch.from_numpy(feats_np).to(dev, torch.bfloat16)
+    bits = torch.from_numpy(bits_np).to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    x = pkg.SparseTensor(feats, coords)
+    km = pkg.SparseConv3d(ws[0]).neighbour_map(x)   # cached on x, as the decoder's blocks share it
+    info = km.info()
+
+    def step():
+        y = pkg.sparse_convnext_block(x, *ws)
+        return pkg.subdivide2(y, bits)
+
+    def timed(fn, n):
+        ts = []
+        for _ in range(n):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) / 1e3)
+        return ts
+
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    fine, _ = step()
+    n_child = int(fine.coords.shape[0])
+    with ClockSampler(dev.index) as clk:
+        launches0 = eng.launch_count()
+        t_step = timed(step, args.steps)
+        launches = eng.launch_count() - launches0
+    dw_out = torch.empty_like(feats)
+    t_dw = timed(lambda: pkg.conv3d_depthwise(km, feats, ws[0], ws[1], out=dw_out), max(args.steps, 5))
+    t_sub = timed(lambda: pkg.subdivide2(x, bits), max(args.steps, 5))
+    eng.synchronize()
+    dw_s, sub_s = statistics.median(t_dw), statistics.median(t_sub)
+    # algorithmic bytes of one depthwise launch: every input row read once,
+    # every output row written once, the tile-padded gather indices, the tile
+    # row list and the weights
+    dw_bytes = 2 * w.n * C * 2 + 4 * info["tile_pairs"] + 4 * 128 * info["num_tiles"] + 27 * C * 2
+    # subdivision: coords, mask and feature rows read once; child coords,
+    # parents and feature rows written once
+    sub_bytes = w.n * (16 + 1 + 2 * C) + n_child * (16 + 4 + 2 * C)
+    hbm = float(peaks["hbm_gbs"])
+    roof = {"bound": "hbm", "kernel": "k_conv_dw<bf16>", "achieved": dw_bytes / dw_s / 1e9, "peak": hbm,
+            "unit": "GB/s", "frac": dw_bytes / dw_s / 1e9 / hbm,
+            "algorithmic_bytes_per_launch": dw_bytes, "traffic": None,
+            "peak_source": f"{peak_src} hbm_gbs (burst: the kernel is timed alone)"}
+    sub_roof = {"bound": "hbm", "kernels": "k_subdiv_count/scan/write + k_gather_rows",
+                "achieved": sub_bytes / sub_s / 1e9, "peak": hbm, "unit": "GB/s",
+                "frac": sub_bytes / sub_s / 1e9 / hbm, "algorithmic_bytes_per_call": sub_bytes,
+                "note": "includes the host read of the child count (one stream synchronize per masked call)"}
+
+    # end to end through the public API: H2D of coords + feats + mask from
+    # pinned memory, map build, block, subdivision, D2H of the child features
+    coords_h = torch.from_numpy(coords_np).pin_memory()
+    feats_h = torch.from_numpy(feats_np).to(torch.bfloat16).pin_memory()
+    bits_h = torch.from_numpy(bits_np).pin_memory()
+    out_h = torch.empty((n_child, C), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        c_d = coords_h.to(dev, non_blocking=True)
+        f_d = feats_h.to(dev, non_blocking=True)
+        b_d = bits_h.to(dev, non_blocking=True)
+        xx = pkg.SparseTensor(f_d, c_d)
+        fine_d, _ = pkg.subdivide2(pkg.sparse_convnext_block(xx, *ws), b_d)
+        out_h.copy_(fine_d.feats, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    t_e2e = timed(e2e_step, max(3, args.steps // 2))
+    e2e_matches = bool(torch.equal(out_h, fine.feats.cpu()))
+
+    # CPU baseline: the oracle's block and subdivision on a bounded sample of
+    # rows (their neighbour lookups still search every voxel), one BLAS thread
+    cpu = None
+    if args.cpu_steps > 0:
+        from threadpoolctl import threadpool_limits
+        from oracle import sparse_conv_ref as R
+        sample = 20000
+        rows = np.arange(sample)
+        f64 = feats.float().cpu().numpy().astype(np.float64)
+        w64 = [t.float().cpu().numpy().astype(np.float64) for t in ws]
+        times = []
+        with threadpool_limits(1):
+            for k in range(1 + args.cpu_steps):
+                t0 = time.perf_counter()
+                kmr = R.kmap_sorted(coords_np, w.spatial_shape, rows=rows)
+                h = R.conv_depthwise(f64, kmr, w64[0], w64[1])
+                h = R.layer_norm(h)
+                h = R.silu(R.layer_norm(h @ w64[2].T + w64[3]))
+                y = h @ w64[4].T + w64[5] + f64[rows]
+                R.subdivide2(coords_np[rows], y, mask_np[rows])
+                if k:
+                    times.append(time.perf_counter() - t0)
+        cpu = {"value": sample * len(times) / sum(times), "unit": "voxels/s", "cores": 1, "kind": "port",
+               "sample": f"first {sample} of {w.n} voxels (ConvNeXt block + subdivision), "
+                         f"{len(times)} timed runs after 1 warm-up, numpy float64, 1 thread"}
+
+    step_s = statistics.median(t_step)
+    line = {
+        "metric": "sparse ConvNeXt decoder block + 2x2x2 subdivision, active voxels/s", "workload": "dec",
+        "value": w.n / step_s, "unit": "voxels/s", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": 1e3 * step_s, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": f"synthetic: BASELINE configs[1] voxels, seeded features and weights, C={C}",
+        "config": {"workload": f"convnext_block_c{C}_subdivide_{w.name}", "voxels": w.n, "channels": C,
+                   "hidden": 4 * C, "children": n_child, "pairs": info["num_pairs"], "l2": L2_NOTE,
+                   "map": "built once per coord set (cached on the tensor), not in the step"},
+        "depthwise_ms": 1e3 * dw_s, "subdivide_ms": 1e3 * sub_s,
+        "roofline": roof, "subdivide_roofline": sub_roof,
+        "cpu_baseline": cpu,
+        "e2e": {"value": w.n / statistics.median(t_e2e), "unit": "voxels/s",
+                "h2d_bytes_per_step": coords_h.numel() * 4 + feats_h.numel() * 2 + bits_h.numel(),
+                "d2h_bytes_per_step": out_h.numel() * 2, "matches_device_api": e2e_matches,
+                "api": "per step: H2D of coords, feats and child mask, map build, sparse_convnext_block, "
+                       "subdivide2, D2H of the child features"},
+        "clocks": clk.summary(),
+        "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def _cpu_chain(idx, w, sample_rows):
     """One CPU step of config `idx` (torch CPU restatement) on the first `sample_rows`
     Morton-ordered voxels; returns (seconds, pairs-in-sample)."""
@@ -1038,7 +1209,7 @@ def run_table(args):
     eng = pkg.get_engine(dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     steps = max(args.steps, 5)
-    for idx in (1, 2, 3, 4, 5):
+    for idx in sorted({int(x) for x in args.configs.split(",") if x.strip()}):
         w = pkg.workloads.make_workload(idx)
         dt = torch.float32 if w.dtype == "f32" else torch.bfloat16
         coords = torch.from_numpy(w.coords).to(dev)
@@ -1086,9 +1257,12 @@ def run_table(args):
         flops = sum(2.0 * ci * co * inf["num_pairs"] for (ci, co), inf in zip(chans, infos))
         gm, gc = statistics.median(t_map), statistics.median(t_conv)
         del maps
-        cpu_runs = [_cpu_chain(idx, w, 400_000) for _ in range(2 + 5)][2:]  # 2 warm-ups, median of 5
-        cpu_s, cpu_n = statistics.median(r[0] for r in cpu_runs), cpu_runs[0][2]
-        cpu_full_ms = 1e3 * cpu_s * (w.n / cpu_n)
+        if args.cpu_steps > 0:
+            cpu_runs = [_cpu_chain(idx, w, 400_000) for _ in range(2 + 5)][2:]  # 2 warm-ups, median of 5
+            cpu_s, cpu_n = statistics.median(r[0] for r in cpu_runs), cpu_runs[0][2]
+            cpu_full_ms = 1e3 * cpu_s * (w.n / cpu_n)
+        else:
+            cpu_n, cpu_full_ms = 0, None
         line = {
             "table": w.name, "voxels": w.n, "pairs": [inf["num_pairs"] for inf in infos],
             "dtype": w.dtype, "gpu_map_ms": gm, "gpu_conv_ms": gc, "gpu_total_ms": gm + gc,
@@ -1097,9 +1271,9 @@ def run_table(args):
             "peak_source": f"{peak_src} bf16_tflops (burst)",
             "gpu_voxels_per_s": w.n / ((gm + gc) * 1e-3),
             "cpu_ms": cpu_full_ms, "cpu_threads": torch.get_num_threads(), "cpu_runs": "median of 5 after 2 warm-ups",
-            "cpu_sample": ("full workload" if cpu_n == w.n else
+            "cpu_sample": ("not run (--cpu-steps 0)" if cpu_full_ms is None else "full workload" if cpu_n == w.n else
                            f"first {cpu_n} Morton-ordered voxels, time scaled by {w.n / cpu_n:.2f}"),
-            "speedup_vs_cpu": cpu_full_ms / (gm + gc), "steps": steps,
+            "speedup_vs_cpu": None if cpu_full_ms is None else cpu_full_ms / (gm + gc), "steps": steps,
             "chain": {1: "map + conv (f32 SIMT path)", 2: "map + conv", 3: "map + conv(LN,SiLU) + conv(+skip)",
                       4: "down map + subm map + up map; down 64->128, subm 128, up 128->64",
                       5: "map + conv"}[idx],
@@ -1122,6 +1296,8 @@ def main():
         return run_c4(args)
     if args.workload == "table":
         return run_table(args)
+    if args.workload == "dec":
+        return run_dec(args)
     return run_ours(args)
 
 

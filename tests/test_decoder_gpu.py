@@ -243,3 +243,20 @@ def test_coords_cache_to_kmap(pkg, oracle, cuda, tmp_path):
     assert np.array_equal(km.export().cpu().numpy(), oracle.kmap_sorted(c4, w.spatial_shape))
     out = pkg.conv3d_depthwise(km, x.feats, torch.ones((8, 27), device=cuda))
     assert out.shape == (w.n, 8)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("c", [12, 16, 24, 64, 96, 200, 256, 1000, 4096])
+@pytest.mark.parametrize("silu", [False, True])
+def test_layernorm_silu_matches_torch(pkg, cuda, dtype, c, silu):
+    """The engine's in-place row LayerNorm (no affine, eps 1e-6) + optional
+    SiLU against torch in float64, over the vectorised widths and the scalar
+    fallback (rows that are not a whole number of 16-byte vectors)."""
+    rng = np.random.default_rng(c)
+    n = 5003
+    x = torch.from_numpy((3 * rng.standard_normal((n, c)) + 1).astype(np.float32)).to(cuda, dtype)
+    ref = torch.nn.functional.layer_norm(x.double(), (c,), eps=1e-6)
+    if silu:
+        ref = torch.nn.functional.silu(ref)
+    y = pkg.layernorm_silu(x.clone(), silu=silu)
+    assert rel_l2(_f64(y), ref.cpu().numpy()) < TOL[dtype]

@@ -9,6 +9,8 @@
 #include "sc_common.cuh"
 #include "sc_internal.h"
 
+#include <type_traits>
+
 namespace sc {
 namespace {
 
@@ -128,13 +130,155 @@ __global__ void k_rownorm(T* __restrict__ x, int64_t n, int c, float eps, int do
   }
 }
 
+// Vectorised rows: L lanes share a row (32 / L rows per warp), each lane
+// holds VPL 16-byte vectors of it in registers, so the row is read once and
+// written once.  Mean and variance are two passes over the registers (the
+// same two-pass statistics as k_rownorm), reduced with xor shuffles inside
+// the L-lane group.  Needs c a multiple of the vector width and 16-byte
+// aligned rows.
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& u, float* f) {
+  if constexpr (sizeof(T) == 4) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y); f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+  } else {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const T* h = reinterpret_cast<const T*>(&w[j]);
+      f[2 * j] = Cvt<T>::to_f(h[0]);
+      f[2 * j + 1] = Cvt<T>::to_f(h[1]);
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack16(const float* f) {
+  if constexpr (sizeof(T) == 4) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+        const __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+        w[j] = *reinterpret_cast<const uint32_t*>(&b);
+      } else {
+        const __half2 b = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+        w[j] = *reinterpret_cast<const uint32_t*>(&b);
+      }
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+template <typename T, int L, int VPL>
+__global__ void __launch_bounds__(256) k_rownorm_vec(T* __restrict__ x, int64_t n, int c, float eps, int do_ln,
+                                                     int do_silu, const T* __restrict__ residual) {
+  constexpr int EPV = 16 / static_cast<int>(sizeof(T));
+  const int lane = threadIdx.x & 31;
+  const int li = lane % L;
+  const int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5)) * (32 / L) + lane / L;
+  const bool live = row < n;
+  const int nvec = c / EPV;
+  float v[VPL][EPV];
+  uint4* xr = reinterpret_cast<uint4*>(x + (live ? row : 0) * c);
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int j = li + k * L;
+    if (live && j < nvec) {
+      unpack16<T>(xr[j], v[k]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) v[k][e] = 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < EPV; ++e) s += v[k][e];
+  }
+  float mean = 0.f, rstd = 1.f;
+  if (do_ln) {
+#pragma unroll
+    for (int o = L / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    mean = s / static_cast<float>(c);
+    float s2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      if (li + k * L < nvec) {
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) {
+          const float d = v[k][e] - mean;
+          s2 += d * d;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = L / 2; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    rstd = rsqrtf(s2 / static_cast<float>(c) + eps);
+  }
+  if (!live) return;
+  const uint4* rr = residual ? reinterpret_cast<const uint4*>(residual + row * c) : nullptr;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int j = li + k * L;
+    if (j >= nvec) continue;
+    float y[EPV], r[EPV];
+    if (rr) unpack16<T>(rr[j], r);
+#pragma unroll
+    for (int e = 0; e < EPV; ++e) {
+      float t = v[k][e];
+      if (do_ln) t = (t - mean) * rstd;
+      if (do_silu) t = silu_f(t);
+      if (rr) t += r[e];
+      y[e] = t;
+    }
+    xr[j] = pack16<T>(y);
+  }
+}
+
+template <typename T, int L, int VPL>
+void launch_rownorm_vec(Handle* h, T* x, int64_t n, int c, float eps, int ln, int silu, const T* res) {
+  const int64_t rows_per_block = 8 * (32 / L);
+  const unsigned grid = static_cast<unsigned>((n + rows_per_block - 1) / rows_per_block);
+  k_rownorm_vec<T, L, VPL><<<grid, 256, 0, h->stream>>>(x, n, c, eps, ln, silu, res);
+}
+
 template <typename T>
 sc_status launch_rownorm(Handle* h, void* x, int64_t n, int c, float eps, int ln, int silu, const void* res) {
-  const int rows_per_block = 8;
-  const unsigned grid = static_cast<unsigned>((n + rows_per_block - 1) / rows_per_block);
+  constexpr int EPV = 16 / static_cast<int>(sizeof(T));
+  const int nvec = c / EPV;
+  const bool vec = c % EPV == 0 && nvec >= 4 && nvec <= 32 * 16 &&
+                   reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(res) % 16 == 0;
+  T* xt = static_cast<T*>(x);
+  const T* rt = static_cast<const T*>(res);
   ++h->launches;
-  k_rownorm<T><<<grid, rows_per_block * 32, 0, h->stream>>>(static_cast<T*>(x), n, c, eps, ln, silu,
-                                                            static_cast<const T*>(res));
+  if (vec) {
+    const int L = nvec >= 32 ? 32 : nvec >= 16 ? 16 : nvec >= 8 ? 8 : 4;
+    const int vpl = (nvec + L - 1) / L;  // <= 2 when L < 32
+    if (L == 4) {
+      if (vpl == 1) launch_rownorm_vec<T, 4, 1>(h, xt, n, c, eps, ln, silu, rt);
+      else launch_rownorm_vec<T, 4, 2>(h, xt, n, c, eps, ln, silu, rt);
+    } else if (L == 8) {
+      if (vpl == 1) launch_rownorm_vec<T, 8, 1>(h, xt, n, c, eps, ln, silu, rt);
+      else launch_rownorm_vec<T, 8, 2>(h, xt, n, c, eps, ln, silu, rt);
+    } else if (L == 16) {
+      if (vpl == 1) launch_rownorm_vec<T, 16, 1>(h, xt, n, c, eps, ln, silu, rt);
+      else launch_rownorm_vec<T, 16, 2>(h, xt, n, c, eps, ln, silu, rt);
+    } else if (vpl == 1) {
+      launch_rownorm_vec<T, 32, 1>(h, xt, n, c, eps, ln, silu, rt);
+    } else if (vpl == 2) {
+      launch_rownorm_vec<T, 32, 2>(h, xt, n, c, eps, ln, silu, rt);
+    } else if (vpl <= 4) {
+      launch_rownorm_vec<T, 32, 4>(h, xt, n, c, eps, ln, silu, rt);
+    } else if (vpl <= 8) {
+      launch_rownorm_vec<T, 32, 8>(h, xt, n, c, eps, ln, silu, rt);
+    } else {
+      launch_rownorm_vec<T, 32, 16>(h, xt, n, c, eps, ln, silu, rt);
+    }
+  } else {
+    const int rows_per_block = 8;
+    const unsigned grid = static_cast<unsigned>((n + rows_per_block - 1) / rows_per_block);
+    k_rownorm<T><<<grid, rows_per_block * 32, 0, h->stream>>>(xt, n, c, eps, ln, silu, rt);
+  }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SC_OK : cuda_error(h, e, "rownorm launch");
 }
