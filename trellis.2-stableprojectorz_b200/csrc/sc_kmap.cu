@@ -53,7 +53,12 @@ __device__ __forceinline__ uint32_t mix64(unsigned long long k) {
 //
 // The block hash is separable: per-axis terms are multiplied by odd constants
 // and xored, then finalised with a 32-bit multiply-xorshift, so a voxel's 27
-// neighbours need only 3 terms per axis plus one finaliser each.
+// neighbours need only 3 terms per axis plus one finaliser each.  The four
+// multipliers are the 32-bit primes of xxHash32 (Y. Collet, PRIME32_1..4);
+// the finaliser is a two-round xorshift-multiply (shifts 15/12/15) from the
+// constant search published with C. Wellons' hash-prospector.  Rehash probes
+// step the key by multiples of 2^64 / golden ratio (the SplitMix64
+// increment) before the MurmurHash3 fmix64 mixer.
 __device__ __forceinline__ uint32_t axis_term(int v, uint32_t mul) { return static_cast<uint32_t>(v) * mul; }
 constexpr uint32_t kMulB = 0x27D4EB2Fu, kMulX = 0x9E3779B1u, kMulY = 0x85EBCA77u, kMulZ = 0xC2B2AE3Du;
 __device__ __forceinline__ uint32_t fin32(uint32_t h) {
