@@ -256,6 +256,22 @@ SC_API sc_status sc_subdivide2(sc_handle* h, const int32_t* coords, int64_t n, c
                         const void* feats, int32_t row_bytes, int32_t* out_coords, int32_t* out_parent,
                         void* out_feats, int64_t capacity, int64_t* n_out);
 
+/* Variable-length scaled dot-product attention (the SLat flow model's sparse
+ * self / cross attention, src/sparse/ops/attention.ts:24-80 with the dense op
+ * of src/dense/ops/attention.ts:2,61): for every sequence b and head h,
+ * out[i, h] = softmax_j(scale * q[i, h] . k[j, h]) v[j, h] over the key rows j
+ * of sequence b.  q / out are [cu_seqlens_q[batch], num_heads, head_dim],
+ * k / v are [cu_seqlens_kv[batch], num_heads, head_dim] device arrays (16-byte
+ * aligned); cu_seqlens_q / cu_seqlens_kv are HOST arrays of batch + 1
+ * non-decreasing offsets starting at 0 (the reference passes Uint32Array
+ * cuSeqlensQ / cuSeqlensKV).  head_dim must be 64; dtype bf16 or f16; f32
+ * accumulation, P rounded to the input type for the second product.  Query
+ * rows of a sequence with no key rows get zeros.  scale is usually
+ * 1 / sqrt(head_dim). */
+SC_API sc_status sc_attention_varlen(sc_handle* h, const void* q, const void* k, const void* v, void* out,
+                              const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_kv, int32_t batch,
+                              int32_t num_heads, int32_t head_dim, float scale, sc_dtype dtype);
+
 /* Row LayerNorm (no affine) + optional SiLU, in place on [n, c] features
  * (src/dense/ops/layer_norm.ts:28-60, src/dense/ops/silu.ts:20-31). */
 SC_API sc_status sc_layernorm_silu(sc_handle* h, void* x, int64_t n, int32_t c, sc_dtype dtype, int32_t apply_silu,

@@ -46,6 +46,8 @@ Functions and the reference lines they follow:
   ``(C,3,3,3,1)`` conv weight as an alternative to the dense one.
 * ``subdivide2`` -- 2x2x2 voxel subdivision with an optional child mask, the
   upsample the TS decoder leaves out (``sparse_unet_vae_decoder.ts:155-175``).
+* ``attention_varlen`` -- per-sequence scaled dot-product attention of the
+  SLat flow model (``src/sparse/ops/attention.ts:24-80``).
 """
 from __future__ import annotations
 
@@ -54,7 +56,7 @@ import numpy as np
 __all__ = [
     "flat_keys", "kmap_bruteforce", "kmap_sorted", "conv_gather", "down2_map",
     "up2_map", "layer_norm", "silu", "resblock", "round_bf16", "offsets27", "dense_conv3d_check",
-    "torch_cpu_kmap", "torch_cpu_conv", "conv_depthwise", "convnext_block", "subdivide2",
+    "torch_cpu_kmap", "torch_cpu_conv", "conv_depthwise", "convnext_block", "subdivide2", "attention_varlen",
 ]
 
 
@@ -307,6 +309,33 @@ def subdivide2(coords, feats, child_mask=None):
     keep = np.ones((n, 8), bool) if child_mask is None else np.asarray(child_mask, bool).reshape(n, 8)
     fine, parent = fine[keep], parent[keep]
     return fine.astype(np.int32), None if feats is None else np.asarray(feats)[parent]
+
+
+def attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_kv=None, scale=None):
+    """Per-sequence scaled dot-product attention, float64
+    (``src/sparse/ops/attention.ts:24-80``: each batch item runs
+    ``O = softmax(Q K^T * scale) V`` of ``src/dense/ops/attention.ts:2,61``
+    with ``scale = 1 / sqrt(D)``; items with no query or no key rows are
+    skipped and keep zeros, ``:50``).  ``q`` ``(N, H, D)``, ``k``/``v``
+    ``(N_kv, H, D)``."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    cq = [int(x) for x in cu_seqlens_q]
+    ck = cq if cu_seqlens_kv is None else [int(x) for x in cu_seqlens_kv]
+    d = q.shape[2]
+    s = 1.0 / np.sqrt(d) if scale is None else float(scale)
+    out = np.zeros_like(q)
+    for b in range(len(cq) - 1):
+        qs, ks = q[cq[b]:cq[b + 1]], k[ck[b]:ck[b + 1]]
+        if len(qs) == 0 or len(ks) == 0:
+            continue
+        logits = np.einsum("ihd,jhd->hij", qs, ks) * s
+        logits -= logits.max(axis=2, keepdims=True)
+        p = np.exp(logits)
+        p /= p.sum(axis=2, keepdims=True)
+        out[cq[b]:cq[b + 1]] = np.einsum("hij,jhd->ihd", p, v[ck[b]:ck[b + 1]])
+    return out
 
 
 def dense_conv3d_check(coords, feats, weight, bias, spatial_shape, batch_size):

@@ -220,3 +220,24 @@ def test_subdivide_oracle_properties(oracle):
     assert len(fm) == mask.sum()
     keep = mask.ravel()
     assert np.array_equal(fm, fine[keep]) and np.array_equal(fmf, ff[keep])
+
+
+def test_attention_oracle_matches_torch_sdpa(oracle):
+    import torch
+    rng = np.random.default_rng(31)
+    lq, lk = [5, 0, 17, 3], [7, 4, 0, 11]
+    cq, ck = np.concatenate([[0], np.cumsum(lq)]), np.concatenate([[0], np.cumsum(lk)])
+    q = rng.standard_normal((cq[-1], 3, 64))
+    k = rng.standard_normal((ck[-1], 3, 64))
+    v = rng.standard_normal((ck[-1], 3, 64))
+    out = oracle.attention_varlen(q, k, v, cq, ck)
+    for b in range(4):
+        s, t = slice(cq[b], cq[b + 1]), slice(ck[b], ck[b + 1])
+        if lq[b] == 0:
+            continue
+        if lk[b] == 0:
+            assert not out[s].any()
+            continue
+        T = lambda x, sl: torch.from_numpy(x[sl]).transpose(0, 1)
+        ref = torch.nn.functional.scaled_dot_product_attention(T(q, s), T(k, t), T(v, t)).transpose(0, 1).numpy()
+        np.testing.assert_allclose(out[s], ref, rtol=1e-10, atol=1e-12)

@@ -4,7 +4,7 @@ A drop-in for the reference sparse-conv operator (``SparseConv3d`` of
 ``src/sparse/ops/conv3d.ts`` / the ``SPARSE_CONV_BACKEND`` module of
 ``trellis2/modules/sparse/conv``): kernel-map construction (hash or one-sweep
 radix sort), a tcgen05 implicit-GEMM conv fed by TMA row gathers and TMA
-weight tiles, a depthwise conv, 2x2x2 subdivision, stride-2 down/up convs, Morton-range sharding across GPUs, and a
+weight tiles, a depthwise conv, 2x2x2 subdivision, varlen attention, stride-2 down/up convs, Morton-range sharding across GPUs, and a
 host-to-host pipeline that overlaps the transfers of consecutive calls.  All compute is in
 ``libsparseconv_b200.so`` (C ABI in ``include/sparse_conv_b200.h``).
 """
@@ -13,7 +13,7 @@ from ._lib import SparseConvError, DuplicateCoordError, CoordRangeError
 from .sparse_conv import (
     Engine, get_engine, KernelMap, build_kmap, concat_kmaps, HaloWait, build_down2, build_up2, conv3d, layernorm_silu,
     SparseTensor, SparseConv3d, SparseConvDown2, SparseConvUp2, sparse_conv3d_forward, sparse_resblock,
-    conv3d_depthwise, sparse_convnext_block, subdivide2,
+    conv3d_depthwise, sparse_convnext_block, subdivide2, sparse_attention,
 )
 from . import coords_io
 from .host_pipeline import HostConvPipeline

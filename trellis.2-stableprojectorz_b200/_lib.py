@@ -95,6 +95,7 @@ _SIGNATURES = {
     "sc_conv3d_up2": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _U32]),
     "sc_conv3d_depthwise": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32]),
     "sc_subdivide2": (_I32, [_P, _P, _I64, _P, _P, _I32, _P, _P, _P, _I64, _P]),
+    "sc_attention_varlen": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _F, _I32]),
     "sc_layernorm_silu": (_I32, [_P, _P, _I64, _I32, _I32, _I32, _F]),
     "sc_peer_alloc": (_I32, [_P, ctypes.c_size_t, _PP, _P]),
     "sc_peer_free": (_I32, [_P, _P]),

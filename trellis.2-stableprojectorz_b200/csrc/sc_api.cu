@@ -530,6 +530,30 @@ sc_status sc_subdivide2(sc_handle* h, const int32_t* coords, int64_t n, const ui
                         n_out);
 }
 
+sc_status sc_attention_varlen(sc_handle* h, const void* q, const void* k, const void* v, void* out,
+                              const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_kv, int32_t batch,
+                              int32_t num_heads, int32_t head_dim, float scale, sc_dtype dtype) {
+  if (!h) return SC_EINVAL;
+  Handle* H = &h->impl;
+  if (head_dim != 64) return sc::set_error(H, SC_EUNSUPPORTED, "attention: head_dim must be 64");
+  if (dtype != SC_BF16 && dtype != SC_F16) return sc::set_error(H, SC_EUNSUPPORTED, "attention: bf16 or f16 only");
+  if (batch < 1 || num_heads < 1 || num_heads > 65535 || !cu_seqlens_q || !cu_seqlens_kv)
+    return sc::set_error(H, SC_EINVAL, "attention: need batch >= 1, 1 <= num_heads <= 65535 and both cu_seqlens");
+  if (cu_seqlens_q[0] != 0 || cu_seqlens_kv[0] != 0)
+    return sc::set_error(H, SC_EINVAL, "attention: cu_seqlens must start at 0");
+  for (int32_t b = 0; b < batch; ++b)
+    if (cu_seqlens_q[b + 1] < cu_seqlens_q[b] || cu_seqlens_kv[b + 1] < cu_seqlens_kv[b])
+      return sc::set_error(H, SC_EINVAL, "attention: cu_seqlens must be non-decreasing");
+  if (!(scale > 0.f)) return sc::set_error(H, SC_EINVAL, "attention: scale must be positive");
+  if (cu_seqlens_q[batch] == 0) return SC_OK;
+  if (!q || !out || (cu_seqlens_kv[batch] > 0 && (!k || !v)))
+    return sc::set_error(H, SC_EINVAL, "attention: null operand");
+  if (!sc::aligned(q, 16) || !sc::aligned(out, 16) || (k && !sc::aligned(k, 16)) || (v && !sc::aligned(v, 16)))
+    return sc::set_error(H, SC_EINVAL, "attention: q, k, v and out must be 16-byte aligned device arrays");
+  sc::DeviceGuard g(H->device);
+  return sc::attention_varlen(H, q, k, v, out, cu_seqlens_q, cu_seqlens_kv, batch, num_heads, scale, dtype);
+}
+
 sc_status sc_layernorm_silu(sc_handle* h, void* x, int64_t n, int32_t c, sc_dtype dtype, int32_t apply_silu,
                             float eps) {
   if (!h) return SC_EINVAL;

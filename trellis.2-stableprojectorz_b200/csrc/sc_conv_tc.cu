@@ -1096,6 +1096,21 @@ __global__ void k_check_gidx(const int32_t* gidx, int64_t total, int64_t n_in, i
 
 }  // namespace
 
+// 3-D tiled tensor map over 16-bit elements with the 128-byte swizzle (the
+// attention kernel's Q, K and V^T tiles); strides in bytes of dims 1 and 2.
+bool make_map_3d(CUtensorMap* m, bool bf16, const void* base, const uint64_t dims[3], const uint64_t strides[2],
+                 const uint32_t box[3]) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  const cuuint64_t st[2] = {strides[0], strides[1]};
+  const cuuint32_t bx[3] = {box[0], box[1], box[2]};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+             const_cast<void*>(base), d, st, bx, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Debug mode: verifies every gather index of the map lies in [-1, n_in).
 sc_status check_gather_bounds(Handle* h, const KMap* km) {
   const int64_t total = km->num_tiles * km->K * kTileRows;

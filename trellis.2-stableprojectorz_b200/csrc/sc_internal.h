@@ -114,6 +114,9 @@ sc_status conv_simt_f32(Handle* h, const KMap* km, const float* feats, const flo
                         const float* residual, float* out, int ci, int co, uint32_t epi, float eps);
 sc_status check_gather_bounds(Handle* h, const KMap* km);
 sc_status layernorm_silu(Handle* h, void* x, int64_t n, int c, sc_dtype dtype, int silu, float eps);
+// variable-length attention, head dim 64 (sc_attn.cu); cu_q / cu_kv are host arrays
+sc_status attention_varlen(Handle* h, const void* q, const void* k, const void* v, void* out, const int32_t* cu_q,
+                           const int32_t* cu_kv, int batch, int heads, float scale, sc_dtype dtype);
 // 2x2x2 subdivision with an optional child mask (sc_subdiv.cu)
 sc_status subdivide2(Handle* h, const int32_t* coords, int64_t n, const uint8_t* child_mask, const void* feats,
                      int row_bytes, int32_t* out_coords, int32_t* out_parent, void* out_feats, int64_t capacity,

@@ -19,6 +19,7 @@ library surface as ``SparseConvError`` (``DuplicateCoordError`` /
 from __future__ import annotations
 
 import collections
+import math
 import ctypes
 import threading
 
@@ -593,3 +594,39 @@ def subdivide2(x, child_mask=None):
     eng.check(eng.lib.sc_subdivide2(eng.handle, _ptr(coords), n, _ptr(mask), _ptr(feats), row_bytes, _ptr(out_c),
                                     _ptr(parent), _ptr(out_f), total, ctypes.byref(cnt)), "sc_subdivide2")
     return SparseTensor(out_f, out_c, None, tuple(s / 2 for s in x.scale)), parent
+
+
+def sparse_attention(q, k, v, cu_seqlens_q, cu_seqlens_kv=None, scale=None, out=None):
+    """Variable-length scaled dot-product attention (``sc_attention_varlen``),
+    the ``sparseAttention`` of ``src/sparse/ops/attention.ts:14-80``.
+
+    ``q`` ``(total_N, H, 64)``, ``k`` / ``v`` ``(total_N_kv, H, 64)`` (bf16 or
+    f16, CUDA); ``cu_seqlens_q`` / ``cu_seqlens_kv`` the ``B + 1`` sequence
+    offsets (any int sequence or tensor; read on the host, as the reference's
+    ``Uint32Array`` are); ``cu_seqlens_kv`` defaults to ``cu_seqlens_q`` (self
+    attention).  ``scale`` defaults to ``1 / sqrt(64)``.  Returns ``(total_N,
+    H, 64)``; query rows of a sequence with no key rows are zero."""
+    if q.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError("sparse_attention takes bf16 or f16 tensors")
+    if not q.is_cuda:
+        raise ValueError("sparse_attention runs on CUDA tensors only")
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3 or k.shape != v.shape or q.shape[1:] != k.shape[1:]:
+        raise ValueError("q must be (N, H, D) and k, v (N_kv, H, D) with the same H and D")
+    cu_q = torch.as_tensor(cu_seqlens_q, dtype=torch.int32).cpu().contiguous()
+    cu_kv = cu_q if cu_seqlens_kv is None else torch.as_tensor(cu_seqlens_kv, dtype=torch.int32).cpu().contiguous()
+    if cu_q.dim() != 1 or cu_kv.shape != cu_q.shape or cu_q.numel() < 2:
+        raise ValueError("cu_seqlens must be 1-D with batch + 1 entries, the same count for q and kv")
+    if int(cu_q[-1]) != q.shape[0] or int(cu_kv[-1]) != k.shape[0]:
+        raise ValueError("cu_seqlens must end at the token counts of q and k/v")
+    heads, d = int(q.shape[1]), int(q.shape[2])
+    q, k, v = q.contiguous(), k.to(q.dtype).contiguous(), v.to(q.dtype).contiguous()
+    if out is None:
+        out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
+    eng = get_engine(q.device)
+    eng.bind_stream()
+    eng.check(eng.lib.sc_attention_varlen(eng.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(out),
+                                          ctypes.c_void_p(cu_q.data_ptr()), ctypes.c_void_p(cu_kv.data_ptr()),
+                                          cu_q.numel() - 1, heads, d, scale, _DTYPES[q.dtype]),
+              "sc_attention_varlen")
+    return out
