@@ -83,11 +83,12 @@ def parse_args():
                          "peers inside its kernel before its first tile (peer-conv-wait) or, on the "
                          "interior+boundary map, before its first boundary tile (peer-interior-first); or NCCL "
                          "all_to_all_single (nccl)")
-    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "table", "dec"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "table", "dec", "attn"], default="c2",
                     help="c2: BASELINE configs[1] (default); c3: configs[2] ResBlock batch, data-parallel; "
                          "c4: configs[3] down/subm/up, Morton-sharded; c5: configs[4] 1024^3, Morton-sharded; "
                          "table: every config on one GPU; dec: the decoder rows (ConvNeXt block with a depthwise "
-                         "conv, 2x2x2 subdivision) on configs[1]'s voxels, one GPU")
+                         "conv, 2x2x2 subdivision) on configs[1]'s voxels, one GPU; attn: varlen attention of the "
+                         "SLat flow model (16 heads of 64, two sequences of 10,000 and 6,384 tokens), one GPU")
     ap.add_argument("--map-mode", choices=["hash", "sort"], default="hash",
                     help="c2 on one GPU / replicas: kernel-map construction by hash probe (default) or radix sort")
     ap.add_argument("--halo-map", action="store_true",
@@ -1162,6 +1163,113 @@ def run_dec(args):
     return 0
 
 
+ATTN_LENS = (10000, 6384)
+ATTN_HEADS = 16
+
+
+def run_attn(args):
+    """Varlen self-attention on one GPU: the SLat flow model's sparse
+    attention (``src/sparse/ops/attention.ts``) over two sequences of 10,000
+    and 6,384 tokens, 16 heads of 64, bf16.  A step is one attention call;
+    device-timed with inputs resident (K/V of one head fit L2, as in the
+    model), `e2e` with the H2D copy of q, k, v and the D2H copy of the output.
+    Not the driver's headline line."""
+    import numpy as np
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    rank, local_rank, world = dist_env()
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"workload": "attn", "unavailable": "the attention row is measured on one GPU"}))
+        return 0
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, peak_src = measured_peaks()
+    eng = pkg.get_engine(dev)
+    lens = list(ATTN_LENS)
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    n_tok, H = cu[-1], ATTN_HEADS
+    rng = np.random.default_rng(7)
+    host = [torch.from_numpy(rng.standard_normal((n_tok, H, 64)).astype(np.float32)).to(torch.bfloat16)
+            for _ in range(3)]
+    q, k, v = (t.to(dev) for t in host)
+    out = torch.empty_like(q)
+    flops = 4.0 * sum(n * n for n in lens) * H * 64
+
+    def timed(fn, n):
+        ts = []
+        for _ in range(n):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) / 1e3)
+        return ts
+
+    step = lambda: pkg.sparse_attention(q, k, v, cu, out=out)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clk:
+        launches0 = eng.launch_count()
+        t_step = timed(step, args.steps)
+        launches = eng.launch_count() - launches0
+    eng.synchronize()
+    step_s = statistics.median(t_step)
+    bf16_peak = float(peaks["bf16_tflops"])
+    roof = {"bound": "tensor", "kernel": "k_attn_fwd<bf16>", "achieved": flops / step_s / 1e12, "peak": bf16_peak,
+            "unit": "TFLOP/s", "frac": flops / step_s / 1e12 / bf16_peak,
+            "flops_per_call": flops, "units": "4 * sum(len^2) * heads * 64 (QK^T and PV), V^T pass included",
+            "traffic": None, "peak_source": f"{peak_src} bf16_tflops (burst)"}
+    # end to end: H2D of q, k, v from pinned memory, attention, D2H of the output
+    pin = [t.pin_memory() for t in host]
+    out_h = torch.empty_like(host[0]).pin_memory()
+
+    def e2e_step():
+        qd, kd, vd = (t.to(dev, non_blocking=True) for t in pin)
+        out_h.copy_(pkg.sparse_attention(qd, kd, vd, cu), non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    t_e2e = statistics.median(timed(e2e_step, max(3, args.steps // 2)))
+    e2e_matches = bool(torch.equal(out_h, out.cpu()))
+    cpu = None
+    if args.cpu_steps > 0:
+        from oracle import sparse_conv_ref as R
+        sample = 256  # query rows of the first sequence against all its keys
+        qs, ks, vs = (t.float().numpy().astype(np.float64) for t in host)
+        times = []
+        for i in range(1 + args.cpu_steps):
+            t0 = time.perf_counter()
+            R.attention_varlen(qs[:sample], ks[:lens[0]], vs[:lens[0]], [0, sample], [0, lens[0]])
+            if i:
+                times.append(time.perf_counter() - t0)
+        per_q = statistics.median(times) / sample          # seconds per query row of the 10k sequence
+        cpu_s = per_q * sum(n * n for n in lens) / lens[0]  # all rows, scaled by key count
+        cpu = {"value": n_tok / cpu_s, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{sample} query rows of the 10,000-token sequence against its keys (numpy float64, "
+                         f"BLAS threads), scaled by query rows x key rows to the whole call"}
+    line = {
+        "metric": "varlen sparse attention tokens/s and TFLOP/s", "workload": "attn",
+        "value": n_tok / step_s, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": 1e3 * step_s, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic: seeded normal q, k, v",
+        "config": {"workload": f"attn_varlen_{'+'.join(map(str, lens))}x{H}h64d", "sequences": lens, "heads": H,
+                   "head_dim": 64, "l2": "inputs resident; K and V of a head (2.6 MB) stay in L2 by design"},
+        "attention_tflops": roof["achieved"], "roofline": roof, "cpu_baseline": cpu,
+        "e2e": {"value": n_tok / t_e2e, "unit": "tokens/s", "h2d_bytes_per_step": 3 * host[0].numel() * 2,
+                "d2h_bytes_per_step": out_h.numel() * 2, "matches_device_api": e2e_matches},
+        "clocks": clk.summary(), "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def _cpu_chain(idx, w, sample_rows):
     """One CPU step of config `idx` (torch CPU restatement) on the first `sample_rows`
     Morton-ordered voxels; returns (seconds, pairs-in-sample)."""
@@ -1298,6 +1406,8 @@ def main():
         return run_table(args)
     if args.workload == "dec":
         return run_dec(args)
+    if args.workload == "attn":
+        return run_attn(args)
     return run_ours(args)
 
 

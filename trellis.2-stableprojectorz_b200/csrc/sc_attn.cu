@@ -7,20 +7,23 @@
 // runs src/dense/ops/attention.ts per sequence; O = softmax(Q K^T / sqrt(D)) V
 // at :2,61).  Q, K, V, O are [tokens, H, 64] rows of bf16 or f16.
 //
-// One CTA per (128-query tile of one sequence, head), 256 threads:
-//   warp 0     TMA producer: the Q tile once, then per 128-key tile the K
-//              tile and the V^T tile into a 3-slot ring
-//   warp 1     TMEM owner and single-thread MMA issuer:
-//              S_j = Q K_j^T  (M 128, N 128, K 64) into TMEM (two buffers),
-//              U_j = P_j V_j  (M 128, N 64, K 128) into TMEM (two buffers),
-//              S_{j+1} is issued before U_j so the softmax of tile j overlaps
-//              the next score MMA
-//   warps 4-7  softmax, one query row per thread (TMEM lane): two passes over
-//              its S row (row max, then p = 2^(s*scale*log2 e - m) and its
-//              sum), P_j as bf16/f16 into shared memory in the MMA's
-//              128B-swizzled K-major layout, and the running output
-//              O <- O * 2^(m_old - m_new) + U kept in registers (folded one
-//              tile late, so U_j's MMA overlaps the softmax of tile j+1)
+// One CTA per (256 query rows of one sequence, head), 384 threads:
+//   warp 0     TMA producer: the two 128-row Q tiles once, then per 128-key
+//              tile the K tile and the V^T tile into a 3-slot ring
+//   warp 1     TMEM owner and single-thread MMA issuer, per key tile j:
+//              O_0 += P_0(j) V_j, S_0(j+1) = Q_0 K_{j+1}^T, then the same for
+//              group 1, so the tensor core serves one softmax group while the
+//              other works (S: M 128, N 128, K 64; PV: M 128, N 64, K 128;
+//              accumulators in tensor memory)
+//   warps 4-7, 8-11  softmax groups 0 and 1, one query row per thread (TMEM
+//              lane): two passes over its S row (row max, then
+//              p = 2^(s*scale*log2 e - m) and its sum), P into shared memory
+//              in the MMA's 128B-swizzled K-major layout.  The output O
+//              accumulates in tensor memory across key tiles; its row max m
+//              moves only when a tile's max exceeds it by more than 2^8
+//              (conditional rescaling, the running-max trick of
+//              FlashAttention-4), and only then is the row of O rescaled
+//              in tensor memory.
 // Every operand the MMA reads is K-major: V is first transposed per head into
 // V^T [H, 64, keys], each sequence starting at a multiple of 8 keys so every
 // TMA inner coordinate is 16-byte aligned.  Key columns past the sequence end
@@ -41,22 +44,27 @@ bool make_map_3d(CUtensorMap* m, bool bf16, const void* base, const uint64_t dim
 namespace {
 
 constexpr int kAttnD = 64;          // head dim
-constexpr int kAttnTile = 128;      // query rows per CTA and keys per step
+constexpr int kAttnTile = 128;      // query rows per softmax group and keys per step
 constexpr int kAttnStages = 3;      // K / V^T ring
-constexpr int kAttnThreads = 256;
+constexpr int kAttnThreads = 384;   // 12 warps: producer, MMA, 2 idle, 2 softmax groups of 4
 constexpr int kTileBytes = kAttnTile * kAttnD * 2;   // 16 KB: Q, K or V^T tile
 constexpr int kPBytes = kAttnTile * kAttnTile * 2;   // 32 KB: P tile (two 64-key atoms)
 // shared-memory plan (1024-byte aligned pieces)
-constexpr int kOffQ = 0;
-constexpr int kOffKV = kOffQ + kTileBytes;                         // stage s: K at +0, V^T at +16 KB
-constexpr int kOffP = kOffKV + kAttnStages * 2 * kTileBytes;       // two P buffers
+constexpr int kOffQ = 0;                                           // Q of group 0, group 1 at +16 KB
+constexpr int kOffKV = kOffQ + 2 * kTileBytes;                     // stage s: K at +0, V^T at +16 KB
+constexpr int kOffP = kOffKV + kAttnStages * 2 * kTileBytes;       // P of group 0, group 1 at +32 KB
 constexpr int kOffBar = kOffP + 2 * kPBytes;
 constexpr int kAttnSmem = kOffBar + 256 + 1024;                    // barriers + alignment slack
-constexpr uint32_t kTmemCols = 512;  // S: [0,128) [128,256); U: [256,320) [320,384)
+constexpr uint32_t kTmemCols = 512;  // S of group g: [128g, 128g+128); O of group g: [256+64g, 320+64g)
+// Conditional rescaling: the running row max used for the exponentials moves
+// only when a tile's max exceeds it by more than 2^8, so most tiles leave the
+// output accumulator in tensor memory untouched; weights stay below 2^8.
+constexpr float kRescaleLog2 = 8.f;
 
-// One per (query tile, head) CTA: the tile's sequence bounds.
+// One per CTA: up to 256 query rows of one sequence (group g takes rows
+// q0 + 128g ..) and the sequence's key rows.
 struct AttnTile {
-  int32_t q0, q1;      // query rows [q0, q1)
+  int32_t q0, q1;      // query rows [q0, min(q0 + 256, q1))
   int32_t k0, k1;      // key rows [k0, k1)
   int32_t kp;          // column of key k0 in V^T (a multiple of 8)
   int32_t pad;
@@ -79,6 +87,14 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int3
       : "memory");
 }
 
+// 2^x with the hardware approximation (2 ulp), subnormal results flushed to
+// zero: softmax weights that small contribute nothing at bf16/f16 precision.
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   if constexpr (std::is_same_v<T, __nv_bfloat16>) {
@@ -87,6 +103,158 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   } else {
     const __half2 v = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&v);
+  }
+}
+
+// Each lane reads 64 consecutive f32 columns of its own TMEM lane (one
+// instruction, one wait).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// One softmax group (four warps, one query row per thread = TMEM lane):
+// for every key tile, the row max of S (two 64-column reads), conditional
+// rescaling of the output accumulator O in tensor memory, the weights
+// p = 2^(s * scale * log2 e - m) as bf16/f16 into the group's P buffer in
+// the 128B-swizzled K-major layout, and the running sum; at the end O / sum
+// to global memory.
+template <typename T>
+__device__ __forceinline__ void softmax_group(const AttnParams& p, const AttnTile& tile, int h, int nk, int g,
+                                              int quad, int lane, uint32_t tmem, uint8_t* smem, uint32_t grp0) {
+  const uint32_t s_full = grp0 + 32u * g, s_empty = s_full + 8, p_full = s_full + 16, pv_done = s_full + 24;
+  const int row = quad * 32 + lane;
+  const int qrow = tile.q0 + g * kAttnTile + row;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+  const uint32_t sa = lane_base + g * 128, oa = lane_base + 256 + g * 64;
+  uint8_t* const prow = smem + kOffP + g * kPBytes + row * 128;
+  float m = -INFINITY, l = 0.f;
+  bool ok = true;
+  auto wait_warp = [&](uint32_t bar, uint32_t parity) -> bool {
+    int w = 1;
+    if (lane == 0) w = mbar_wait(bar, parity, p.err) ? 1 : 0;
+    return __shfl_sync(0xffffffffu, w, 0) != 0;
+  };
+  for (int j = 0; j < nk; ++j) {
+    const int valid = min(kAttnTile, tile.k1 - (tile.k0 + j * kAttnTile));  // key columns in the sequence
+    const bool full = valid == kAttnTile;                                    // warp-uniform
+    if (!wait_warp(s_full, j & 1)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    // eight independent max chains (a single chain is 128 dependent steps)
+    float mxv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) mxv[k] = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kAttnTile / 64; ++c) {
+      float s[64];
+      tmem_ld64(sa + c * 64, s);
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) mxv[i & 7] = fmaxf(mxv[i & 7], s[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) mxv[i & 7] = (c * 64 + i < valid) ? fmaxf(mxv[i & 7], s[i]) : mxv[i & 7];
+      }
+    }
+    const float mx = fmaxf(fmaxf(fmaxf(mxv[0], mxv[1]), fmaxf(mxv[2], mxv[3])),
+                           fmaxf(fmaxf(mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7])));
+    const float m_tile = mx * p.scale_log2;
+    const bool move = m_tile > m + kRescaleLog2;  // always true on the first tile (m = -inf)
+    const float m_new = move ? m_tile : m;
+    const float alpha = move ? ex2_ftz(m - m_new) : 1.f;
+    // P_g(j-1) has been multiplied and O_g updated before the buffer and O are touched
+    if (j > 0) {
+      if (!wait_warp(pv_done, (j - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, move)) {
+        float o[64];
+        tmem_ld64(oa, o);
+        uint32_t w[32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[half * 32 + i] * alpha);
+          tmem_st32(oa + half * 32, w);
+        }
+        tmem_wait_st();
+      }
+    }
+    float sumv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sumv[k] = 0.f;
+#pragma unroll
+    for (int c = 0; c < kAttnTile / 64; ++c) {
+      float s[64];
+      tmem_ld64(sa + c * 64, s);
+      if (!full) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) s[i] = (c * 64 + i < valid) ? s[i] : -INFINITY;  // 2^-inf = 0
+      }
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 64; i += 2) {
+        const float p0 = ex2_ftz(fmaf(s[i], p.scale_log2, -m_new));
+        const float p1 = ex2_ftz(fmaf(s[i + 1], p.scale_log2, -m_new));
+        sumv[(i >> 1) & 7] += p0 + p1;
+        pk[i / 2] = pack2<T>(p0, p1);
+      }
+      // 64 keys = one 128-byte row of atom c, eight 16-byte chunks in the 128B swizzle
+      uint8_t* const arow = prow + c * (kPBytes / 2);
+#pragma unroll
+      for (int q8 = 0; q8 < 8; ++q8)
+        *reinterpret_cast<uint4*>(arow + ((q8 ^ (row & 7)) << 4)) =
+            make_uint4(pk[4 * q8], pk[4 * q8 + 1], pk[4 * q8 + 2], pk[4 * q8 + 3]);
+    }
+    tc_fence_before();
+    mbar_arrive(s_empty);        // S_g(j) is read
+    fence_proxy_async_smem();    // P_g(j) (generic stores) is visible to the MMA's async reads
+    mbar_arrive(p_full);         // also orders the O rescale (tcgen05.st) before PV_g(j)
+    const float sum = ((sumv[0] + sumv[1]) + (sumv[2] + sumv[3])) + ((sumv[4] + sumv[5]) + (sumv[6] + sumv[7]));
+    l = fmaf(l, alpha, sum);
+    m = m_new;
+  }
+  float o[64];
+  bool have = false;
+  if (ok && nk > 0 && wait_warp(pv_done, (nk - 1) & 1)) {
+    tc_fence_after();
+    tmem_ld64(oa, o);
+    have = true;
+  }
+  if (qrow < tile.q1) {
+    const float inv = (have && l > 0.f) ? 1.f / l : 0.f;
+    T* dst = static_cast<T*>(p.out) + (static_cast<int64_t>(qrow) * p.heads + h) * kAttnD;
+#pragma unroll
+    for (int c = 0; c < kAttnD / 8; ++c) {
+      uint32_t w4[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        w4[k] = have ? pack2<T>(o[8 * c + 2 * k] * inv, o[8 * c + 2 * k + 1] * inv) : 0u;
+      reinterpret_cast<uint4*>(dst)[c] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
   }
 }
 
@@ -100,28 +268,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 24);
   const uint32_t bar0 = smem_u32(bars);
+  // barriers: q_full, kv_full[3], kv_empty[3], then per group g: s_full, s_empty, p_full, pv_done
   const uint32_t q_full = bar0;
   const uint32_t kv_full0 = bar0 + 8, kv_empty0 = bar0 + 8 * (1 + kAttnStages);
-  const uint32_t s_full0 = bar0 + 8 * (1 + 2 * kAttnStages), s_empty0 = s_full0 + 16;
-  const uint32_t p_full0 = s_empty0 + 16, u_full0 = p_full0 + 16, u_empty0 = u_full0 + 16;
-  const uint32_t done_bar = u_empty0 + 16;
+  const uint32_t grp0 = bar0 + 8 * (1 + 2 * kAttnStages);  // group g's four barriers at grp0 + 32g
+  const uint32_t done_bar = grp0 + 64;
+  auto s_full = [&](int g) { return grp0 + 32u * g; };
+  auto s_empty = [&](int g) { return grp0 + 32u * g + 8; };
+  auto p_full = [&](int g) { return grp0 + 32u * g + 16; };
+  auto pv_done = [&](int g) { return grp0 + 32u * g + 24; };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const AttnTile tile = p.tiles[blockIdx.x];
   const int h = blockIdx.y;
   const int nk = (tile.k1 - tile.k0 + kAttnTile - 1) / kAttnTile;  // key tiles (0: empty key sequence)
+  const int ngroups = tile.q0 + kAttnTile < tile.q1 ? 2 : 1;       // the second group may have no rows
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kAttnStages; ++s) {
-      mbar_init(kv_full0 + 8 * s, 1);
-      mbar_init(kv_empty0 + 8 * s, 1);
+    for (int st = 0; st < kAttnStages; ++st) {
+      mbar_init(kv_full0 + 8 * st, 1);
+      mbar_init(kv_empty0 + 8 * st, 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(s_full0 + 8 * b, 1);
-      mbar_init(s_empty0 + 8 * b, 128);
-      mbar_init(p_full0 + 8 * b, 128);
-      mbar_init(u_full0 + 8 * b, 1);
-      mbar_init(u_empty0 + 8 * b, 128);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(s_full(g), 1);
+      mbar_init(s_empty(g), 128);
+      mbar_init(p_full(g), 128);
+      mbar_init(pv_done(g), 1);
     }
     mbar_init(done_bar, 1);
     fence_mbar_init();
@@ -141,8 +313,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmVt);
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      tma_load_3d(sbase + kOffQ, &tmQ, 0, h, tile.q0, q_full);
+      mbar_arrive_expect_tx(q_full, ngroups * kTileBytes);
+      for (int g = 0; g < ngroups; ++g)
+        tma_load_3d(sbase + kOffQ + g * kTileBytes, &tmQ, 0, h, tile.q0 + g * kAttnTile, q_full);
       for (int j = 0; j < nk; ++j) {
         const int st = j % kAttnStages, n = j / kAttnStages;
         if (!mbar_wait(kv_empty0 + 8 * st, (n & 1) ^ 1, p.err)) break;
@@ -156,144 +329,60 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
+    // Per key tile j: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1): while one group
+    // runs its softmax the tensor core works for the other.
     if (lane == 0 && nk > 0) {
       const bool bf16 = std::is_same_v<T, __nv_bfloat16>;
       const uint32_t id_s = idesc_f16(128, 128, bf16), id_u = idesc_f16(128, 64, bf16);
-      bool ok = mbar_wait(q_full, 0, p.err);
-      auto issue_s = [&](int j) -> bool {  // S_j = Q K_j^T
-        const int st = j % kAttnStages, b = j & 1;
-        if (!mbar_wait(kv_full0 + 8 * st, (j / kAttnStages) & 1, p.err)) return false;
-        if (!mbar_wait(s_empty0 + 8 * b, ((j >> 1) & 1) ^ 1, p.err)) return false;
-        tc_fence_after();
-        const uint32_t kb = sbase + kOffKV + st * 2 * kTileBytes;
+      auto issue_s = [&](int g, int j) {  // S_g(j) = Q_g K_j^T; K_j landed and S_g(j-1) was read
+        const uint32_t kb = sbase + kOffKV + (j % kAttnStages) * 2 * kTileBytes;
+        const uint32_t qb = sbase + kOffQ + g * kTileBytes;
 #pragma unroll
         for (int k = 0; k < kAttnD / 16; ++k)
-          tc_mma_f16(tmem + b * 128, smem_desc(sbase + kOffQ + 32u * k, 1024, 2), smem_desc(kb + 32u * k, 1024, 2),
-                     id_s, k > 0 ? 1u : 0u);
-        tc_commit(s_full0 + 8 * b);
-        return true;
+          tc_mma_f16(tmem + g * 128, smem_desc(qb + 32u * k, 1024, 2), smem_desc(kb + 32u * k, 1024, 2), id_s,
+                     k > 0 ? 1u : 0u);
+        tc_commit(s_full(g));
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < nk; ++j) {
-        const int st = j % kAttnStages, b = j & 1;
-        if (j + 1 < nk && !issue_s(j + 1)) break;
-        if (!mbar_wait(p_full0 + 8 * b, (j >> 1) & 1, p.err)) break;
-        if (!mbar_wait(u_empty0 + 8 * b, ((j >> 1) & 1) ^ 1, p.err)) break;
-        tc_fence_after();
-        const uint32_t pb = sbase + kOffP + b * kPBytes;
-        const uint32_t vb = sbase + kOffKV + st * 2 * kTileBytes + kTileBytes;
+      auto issue_pv = [&](int g, int j) {  // O_g (+)= P_g(j) V_j
+        const uint32_t pb = sbase + kOffP + g * kPBytes;
+        const uint32_t vb = sbase + kOffKV + (j % kAttnStages) * 2 * kTileBytes + kTileBytes;
 #pragma unroll
         for (int k = 0; k < kAttnTile / 16; ++k) {
           const uint32_t atom = static_cast<uint32_t>(k >> 2), off = 32u * (k & 3);
-          tc_mma_f16(tmem + 256 + b * 64, smem_desc(pb + atom * (kPBytes / 2) + off, 1024, 2),
-                     smem_desc(vb + atom * (kTileBytes / 2) + off, 1024, 2), id_u, k > 0 ? 1u : 0u);
+          tc_mma_f16(tmem + 256 + g * 64, smem_desc(pb + atom * (kPBytes / 2) + off, 1024, 2),
+                     smem_desc(vb + atom * (kTileBytes / 2) + off, 1024, 2), id_u, (j > 0 || k > 0) ? 1u : 0u);
         }
-        tc_commit(u_full0 + 8 * b);
-        tc_commit(kv_empty0 + 8 * st);  // K_j and V_j are no longer read
+        tc_commit(pv_done(g));
+      };
+      bool ok = mbar_wait(q_full, 0, p.err) && mbar_wait(kv_full0, 0, p.err);
+      if (ok) {
+        tc_fence_after();
+        for (int g = 0; g < ngroups; ++g) issue_s(g, 0);
+      }
+      for (int j = 0; ok && j < nk; ++j) {
+        const bool next = j + 1 < nk;
+        if (next && !mbar_wait(kv_full0 + 8 * ((j + 1) % kAttnStages), ((j + 1) / kAttnStages) & 1, p.err)) break;
+        for (int g = 0; g < ngroups && ok; ++g) {
+          ok = mbar_wait(p_full(g), j & 1, p.err);  // P_g(j) written (and O_g rescaled if needed)
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(g, j);
+          if (next) {
+            ok = mbar_wait(s_empty(g), j & 1, p.err);  // S_g(j) read
+            if (!ok) break;
+            tc_fence_after();
+            issue_s(g, j + 1);
+          }
+        }
+        tc_commit(kv_empty0 + 8 * (j % kAttnStages));  // K_j and V_j are no longer read
       }
       // every MMA issued must finish before TMEM is released
       tc_commit(done_bar);
       mbar_wait(done_bar, 0, p.err);
     }
-  } else if (warp >= 4) {
+  } else if (warp >= 4 && (warp - 4) / 4 < ngroups) {
     // ------------------------------------------------------------ softmax
-    const int quad = warp & 3;
-    const int row = quad * 32 + lane;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    const int qrow = tile.q0 + row;
-    float o[kAttnD];
-#pragma unroll
-    for (int d = 0; d < kAttnD; ++d) o[d] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
-    bool ok = true;
-    uint8_t* const pbase = smem + kOffP;
-    // folds U_j (written by the MMA for tile j) into o with alpha_j
-    auto fold = [&](int j, float alpha) -> bool {
-      const int b = j & 1;
-      int w = 1;
-      if (lane == 0) w = mbar_wait_sleep<256>(u_full0 + 8 * b, (j >> 1) & 1, p.err) ? 1 : 0;
-      w = __shfl_sync(0xffffffffu, w, 0);
-      if (!w) return false;
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < kAttnD / 32; ++c) {
-        float u[32];
-        tmem_ld32(lane_base + 256 + b * 64 + c * 32, u);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha, u[i]);
-      }
-      tc_fence_before();
-      mbar_arrive(u_empty0 + 8 * b);
-      return true;
-    };
-    for (int j = 0; j < nk; ++j) {
-      const int b = j & 1;
-      const int kbeg = tile.k0 + j * kAttnTile;
-      const int valid = min(kAttnTile, tile.k1 - kbeg);  // key columns of this tile in the sequence
-      int w = 1;
-      if (lane == 0) w = mbar_wait_sleep<256>(s_full0 + 8 * b, (j >> 1) & 1, p.err) ? 1 : 0;
-      w = __shfl_sync(0xffffffffu, w, 0);
-      if (!w) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t sa = lane_base + b * 128;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kAttnTile / 32; ++c) {
-        float s[32];
-        tmem_ld32(sa + c * 32, s);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mx = (c * 32 + i < valid) ? fmaxf(mx, s[i]) : mx;
-      }
-      const float m_new = fmaxf(m, mx * p.scale_log2);
-      float sum = 0.f;
-      uint8_t* const prow = pbase + b * kPBytes + row * 128;
-#pragma unroll
-      for (int c = 0; c < kAttnTile / 32; ++c) {
-        float s[32];
-        tmem_ld32(sa + c * 32, s);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = (c * 32 + i < valid) ? exp2f(fmaf(s[i], p.scale_log2, -m_new)) : 0.f;
-          const float p1 = (c * 32 + i + 1 < valid) ? exp2f(fmaf(s[i + 1], p.scale_log2, -m_new)) : 0.f;
-          sum += p0 + p1;
-          pk[i / 2] = pack2<T>(p0, p1);
-        }
-        // 32 keys = four 16-byte chunks of the row, in the 128B swizzle of atom c / 2
-        uint8_t* const arow = prow + (c >> 1) * (kPBytes / 2);
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int chunk = (c & 1) * 4 + q4;
-          *reinterpret_cast<uint4*>(arow + ((chunk ^ (row & 7)) << 4)) =
-              make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(s_empty0 + 8 * b);   // S_j is read
-      fence_proxy_async_smem();        // P_j (generic stores) is visible to the MMA's async reads
-      mbar_arrive(p_full0 + 8 * b);
-      const float alpha = exp2f(m - m_new);
-      l = fmaf(l, alpha, sum);
-      m = m_new;
-      if (j > 0 && !fold(j - 1, alpha_prev)) {
-        ok = false;
-        break;
-      }
-      alpha_prev = alpha;
-    }
-    if (ok && nk > 0) ok = fold(nk - 1, alpha_prev);
-    if (qrow < tile.q1) {
-      const float inv = (ok && l > 0.f) ? 1.f / l : 0.f;
-      T* dst = static_cast<T*>(p.out) + (static_cast<int64_t>(qrow) * p.heads + h) * kAttnD;
-#pragma unroll
-      for (int c = 0; c < kAttnD / 8; ++c)
-        reinterpret_cast<uint4*>(dst)[c] =
-            make_uint4(pack2<T>(o[8 * c] * inv, o[8 * c + 1] * inv), pack2<T>(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
-                       pack2<T>(o[8 * c + 4] * inv, o[8 * c + 5] * inv), pack2<T>(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
-    }
+    softmax_group<T>(p, tile, h, nk, (warp - 4) / 4, warp & 3, lane, tmem, smem, grp0);
   }
   tc_fence_before();
   __syncthreads();
@@ -344,8 +433,8 @@ sc_status launch_attn(Handle* h, const void* q, const void* k, const void* v, vo
     const int32_t kp = static_cast<int32_t>(cols);
     for (int64_t t = cu_kv[b]; t < cu_kv[b + 1]; ++t) col[t] = static_cast<int32_t>(kp + (t - cu_kv[b]));
     cols += ((cu_kv[b + 1] - cu_kv[b]) + 7) / 8 * 8;
-    for (int32_t q0 = cu_q[b]; q0 < cu_q[b + 1]; q0 += kAttnTile)
-      tiles.push_back(AttnTile{q0, std::min(q0 + kAttnTile, cu_q[b + 1]), cu_kv[b], cu_kv[b + 1], kp, 0});
+    for (int32_t q0 = cu_q[b]; q0 < cu_q[b + 1]; q0 += 2 * kAttnTile)
+      tiles.push_back(AttnTile{q0, cu_q[b + 1], cu_kv[b], cu_kv[b + 1], kp, 0});
   }
   if (tiles.empty()) return SC_OK;
   if (cols >= (1ll << 31)) return set_error(h, SC_EINVAL, "attention: too many key tokens");
