@@ -223,3 +223,29 @@ def test_conv_cta_limit_gives_same_result(pkg, cuda):
             assert torch.equal(pkg.conv3d(km, f, W), ref)
     finally:
         eng.set_conv_ctas(0)
+
+
+@pytest.mark.parametrize("ci,co", [(256, 256), (128, 128), (32, 32)])
+def test_map_built_on_one_stream_used_on_another(pkg, cuda, ci, co):
+    """A map is complete when its build's stream work is: its work orders
+    (one per tiles-per-item choice, used by convs with Co > 128, Co <= 128 and
+    Ci = Co = 32) are written by the build itself, so a conv on a second
+    stream that waits only for the build matches a conv on the first."""
+    w = pkg.workloads.make_workload(2, scale=0.2)
+    rng = np.random.default_rng(ci)
+    c = torch.from_numpy(w.coords).to(cuda)
+    f = torch.from_numpy(rng.standard_normal((w.n, ci)).astype(np.float32)).to(cuda, torch.bfloat16)
+    W = torch.from_numpy((rng.standard_normal((co, 3, 3, 3, ci)) / np.sqrt(27 * ci)).astype(np.float32)).to(
+        cuda, torch.bfloat16)
+    ref = pkg.conv3d(pkg.build_kmap(c), f, W)
+    sa, sb = torch.cuda.Stream(), torch.cuda.Stream()
+    sa.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(sa):
+        km = pkg.build_kmap(c, check=False)
+    sb.wait_stream(sa)
+    with torch.cuda.stream(sb):
+        out = pkg.conv3d(km, f, W)
+    torch.cuda.current_stream().wait_stream(sb)
+    torch.cuda.synchronize()
+    km.check()
+    assert torch.equal(out, ref)

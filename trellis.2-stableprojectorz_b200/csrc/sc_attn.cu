@@ -24,6 +24,10 @@
 //              (conditional rescaling, the running-max trick of
 //              FlashAttention-4), and only then is the row of O rescaled
 //              in tensor memory.
+// Measured on B200 (32k tokens x 16 heads): 532 TFLOP/s.  Computing one in
+// eight / four / two of the weights with a cubic 2^f polynomial on the FMA
+// pipe instead of ex2 (FlashAttention-4's offload) measured 507 / 492 / 433:
+// the softmax here is bound by instruction issue, not by the ex2 unit.
 // Every operand the MMA reads is K-major: V is first transposed per head into
 // V^T [H, 64, keys], each sequence starting at a multiple of 8 keys so every
 // TMA inner coordinate is 16-byte aligned.  Key columns past the sequence end
