@@ -121,6 +121,13 @@ __device__ __forceinline__ unsigned long long add_f2(unsigned long long a, unsig
   return d;
 }
 
+// max(a, b, c) in one instruction (three-input max.f32 of sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   if constexpr (std::is_same_v<T, __nv_bfloat16>) {
@@ -197,7 +204,7 @@ __device__ __forceinline__ void softmax_group(const AttnParams& p, const AttnTil
       tmem_ld64(sa + c * 64, s);
       if (full) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) mxv[i & 7] = fmaxf(mxv[i & 7], s[i]);
+        for (int i = 0; i < 64; i += 2) mxv[(i >> 1) & 7] = max3(mxv[(i >> 1) & 7], s[i], s[i + 1]);
       } else {
 #pragma unroll
         for (int i = 0; i < 64; ++i) mxv[i & 7] = (c * 64 + i < valid) ? fmaxf(mxv[i & 7], s[i]) : mxv[i & 7];
