@@ -29,6 +29,10 @@
 // eight / four / two of the weights with a cubic 2^f polynomial on the FMA
 // pipe instead of ex2 (FlashAttention-4's offload) measured 507 / 492 / 433:
 // the softmax here is bound by instruction issue, not by the ex2 unit.
+// 64-key tiles with S double-buffered per group (S_g(j+2) issued right after
+// PV_g(j), so a group never waits for its next S) measured 428: the fixed
+// per-tile costs (barrier waits, fences, row-max tail) double, and an N = 64
+// product reads more shared memory per FLOP than N = 128.
 // Every operand the MMA reads is K-major: V is first transposed per head into
 // V^T [H, 64, keys], each sequence starting at a multiple of 8 keys so every
 // TMA inner coordinate is 16-byte aligned.  Key columns past the sequence end
