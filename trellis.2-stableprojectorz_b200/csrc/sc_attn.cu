@@ -11,24 +11,31 @@
 //   warp 0     TMA producer: the two 128-row Q tiles once, then per 128-key
 //              tile the K tile and the V^T tile into a 3-slot ring
 //   warp 1     TMEM owner and single-thread MMA issuer, per key tile j:
-//              O_0 += P_0(j) V_j, S_0(j+1) = Q_0 K_{j+1}^T, then the same for
-//              group 1, so the tensor core serves one softmax group while the
-//              other works (S: M 128, N 128, K 64; PV: M 128, N 64, K 128;
-//              accumulators in tensor memory)
+//              S_0(j+1) = Q_0 K_{j+1}^T, then O_0 += P_0(j) V_j, then the same
+//              for group 1, so the tensor core serves one softmax group while
+//              the other works; the next S goes first because the group waits
+//              for it, while O is needed only by a rescale and P's columns
+//              only after the next tile's row max (S: M 128, N 128, K 64;
+//              PV: M 128, N 64, K 128; accumulators in tensor memory; P V
+//              reads P, its A operand, from tensor memory and V^T from
+//              shared memory)
 //   warps 4-7, 8-11  softmax groups 0 and 1, one query row per thread (TMEM
 //              lane): two passes over its S row (row max, then
-//              p = 2^(s*scale*log2 e - m) and its sum), P into shared memory
-//              in the MMA's 128B-swizzled K-major layout.  The output O
+//              p = 2^(s*scale*log2 e - m) and its sum), P as packed bf16/f16
+//              pairs into the group's tensor-memory columns.  The output O
 //              accumulates in tensor memory across key tiles; its row max m
 //              moves only when a tile's max exceeds it by more than 2^8
 //              (conditional rescaling, the running-max trick of
 //              FlashAttention-4), and only then is the row of O rescaled
 //              in tensor memory.
-// Measured on B200 (32k tokens x 16 heads): 540 TFLOP/s (532 before the
-// packed f32x2 arithmetic of the weight loop).  Computing one in
+// Measured on B200 (32k tokens x 16 heads): 625 TFLOP/s; 563 with the
+// product P V issued before the next S instead of after; 540 with P staged
+// in shared memory in the 128B swizzle (eight 16-byte stores per 64 keys and
+// a proxy fence per tile instead of one tcgen05.st), 532 before the packed
+// f32x2 arithmetic of the weight loop.  Computing one in
 // eight / four / two of the weights with a cubic 2^f polynomial on the FMA
 // pipe instead of ex2 (FlashAttention-4's offload) measured 507 / 492 / 433:
-// the softmax here is bound by instruction issue, not by the ex2 unit.
+// the softmax was then bound by instruction issue, not by the ex2 unit.
 // 64-key tiles with S double-buffered per group (S_g(j+2) issued right after
 // PV_g(j), so a group never waits for its next S) measured 428: the fixed
 // per-tile costs (barrier waits, fences, row-max tail) double, and an N = 64
@@ -57,14 +64,14 @@ constexpr int kAttnTile = 128;      // query rows per softmax group and keys per
 constexpr int kAttnStages = 3;      // K / V^T ring
 constexpr int kAttnThreads = 384;   // 12 warps: producer, MMA, 2 idle, 2 softmax groups of 4
 constexpr int kTileBytes = kAttnTile * kAttnD * 2;   // 16 KB: Q, K or V^T tile
-constexpr int kPBytes = kAttnTile * kAttnTile * 2;   // 32 KB: P tile (two 64-key atoms)
 // shared-memory plan (1024-byte aligned pieces)
 constexpr int kOffQ = 0;                                           // Q of group 0, group 1 at +16 KB
 constexpr int kOffKV = kOffQ + 2 * kTileBytes;                     // stage s: K at +0, V^T at +16 KB
-constexpr int kOffP = kOffKV + kAttnStages * 2 * kTileBytes;       // P of group 0, group 1 at +32 KB
-constexpr int kOffBar = kOffP + 2 * kPBytes;
+constexpr int kOffBar = kOffKV + kAttnStages * 2 * kTileBytes;
 constexpr int kAttnSmem = kOffBar + 256 + 1024;                    // barriers + alignment slack
-constexpr uint32_t kTmemCols = 512;  // S of group g: [128g, 128g+128); O of group g: [256+64g, 320+64g)
+// tensor memory of group g: S at [128g, 128g+128), O at [256+64g, 320+64g),
+// P (two 16-bit weights per 32-bit column) at [384+64g, 448+64g)
+constexpr uint32_t kTmemCols = 512;
 // Conditional rescaling: the running row max used for the exponentials moves
 // only when a tile's max exceeds it by more than 2^8, so most tiles leave the
 // output accumulator in tensor memory untouched; weights stay below 2^8.
@@ -171,18 +178,17 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
 // One softmax group (four warps, one query row per thread = TMEM lane):
 // for every key tile, the row max of S (two 64-column reads), conditional
 // rescaling of the output accumulator O in tensor memory, the weights
-// p = 2^(s * scale * log2 e - m) as bf16/f16 into the group's P buffer in
-// the 128B-swizzled K-major layout, and the running sum; at the end O / sum
-// to global memory.
+// p = 2^(s * scale * log2 e - m) as bf16/f16 pairs into the group's P
+// columns of tensor memory (lane = query row, the A operand layout of the
+// second product), and the running sum; at the end O / sum to global memory.
 template <typename T>
 __device__ __forceinline__ void softmax_group(const AttnParams& p, const AttnTile& tile, int h, int nk, int g,
-                                              int quad, int lane, uint32_t tmem, uint8_t* smem, uint32_t grp0) {
+                                              int quad, int lane, uint32_t tmem, uint32_t grp0) {
   const uint32_t s_full = grp0 + 32u * g, s_empty = s_full + 8, p_full = s_full + 16, pv_done = s_full + 24;
   const int row = quad * 32 + lane;
   const int qrow = tile.q0 + g * kAttnTile + row;
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
   const uint32_t sa = lane_base + g * 128, oa = lane_base + 256 + g * 64;
-  uint8_t* const prow = smem + kOffP + g * kPBytes + row * 128;
   float m = -INFINITY, l = 0.f;
   bool ok = true;
   auto wait_warp = [&](uint32_t bar, uint32_t parity) -> bool {
@@ -220,7 +226,7 @@ __device__ __forceinline__ void softmax_group(const AttnParams& p, const AttnTil
     const bool move = m_tile > m + kRescaleLog2;  // always true on the first tile (m = -inf)
     const float m_new = move ? m_tile : m;
     const float alpha = move ? ex2_ftz(m - m_new) : 1.f;
-    // P_g(j-1) has been multiplied and O_g updated before the buffer and O are touched
+    // P_g(j-1) has been multiplied and O_g updated before P's columns and O are touched
     if (j > 0) {
       if (!wait_warp(pv_done, (j - 1) & 1)) {
         ok = false;
@@ -262,17 +268,12 @@ __device__ __forceinline__ void softmax_group(const AttnParams& p, const AttnTil
         sumv[(i >> 1) & 3] = add_f2(sumv[(i >> 1) & 3], pp);
         pk[i / 2] = pack2<T>(p0, p1);
       }
-      // 64 keys = one 128-byte row of atom c, eight 16-byte chunks in the 128B swizzle
-      uint8_t* const arow = prow + c * (kPBytes / 2);
-#pragma unroll
-      for (int q8 = 0; q8 < 8; ++q8)
-        *reinterpret_cast<uint4*>(arow + ((q8 ^ (row & 7)) << 4)) =
-            make_uint4(pk[4 * q8], pk[4 * q8 + 1], pk[4 * q8 + 2], pk[4 * q8 + 3]);
+      tmem_st32(lane_base + 384u + g * 64 + 32u * c, pk);  // keys 64c .. 64c+63
     }
+    tmem_wait_st();
     tc_fence_before();
     mbar_arrive(s_empty);        // S_g(j) is read
-    fence_proxy_async_smem();    // P_g(j) (generic stores) is visible to the MMA's async reads
-    mbar_arrive(p_full);         // also orders the O rescale (tcgen05.st) before PV_g(j)
+    mbar_arrive(p_full);         // P_g(j) and the O rescale (tcgen05.st) are complete
     const unsigned long long s2 = add_f2(add_f2(sumv[0], sumv[1]), add_f2(sumv[2], sumv[3]));
     float sa2, sb2;
     f2_split(s2, sa2, sb2);
@@ -372,7 +373,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    // Per key tile j: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1): while one group
+    // Per key tile j: S_0(j+1), PV_0(j), S_1(j+1), PV_1(j): while one group
     // runs its softmax the tensor core works for the other.
     if (lane == 0 && nk > 0) {
       const bool bf16 = std::is_same_v<T, __nv_bfloat16>;
@@ -387,13 +388,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_commit(s_full(g));
       };
       auto issue_pv = [&](int g, int j) {  // O_g (+)= P_g(j) V_j
-        const uint32_t pb = sbase + kOffP + g * kPBytes;
         const uint32_t vb = sbase + kOffKV + (j % kAttnStages) * 2 * kTileBytes + kTileBytes;
 #pragma unroll
         for (int k = 0; k < kAttnTile / 16; ++k) {
           const uint32_t atom = static_cast<uint32_t>(k >> 2), off = 32u * (k & 3);
-          tc_mma_f16(tmem + 256 + g * 64, smem_desc(pb + atom * (kPBytes / 2) + off, 1024, 2),
-                     smem_desc(vb + atom * (kTileBytes / 2) + off, 1024, 2), id_u, (j > 0 || k > 0) ? 1u : 0u);
+          tc_mma_f16_tmem_a(tmem + 256 + g * 64, tmem + 384u + g * 64 + 8u * k,
+                            smem_desc(vb + atom * (kTileBytes / 2) + off, 1024, 2), id_u, (j > 0 || k > 0) ? 1u : 0u);
         }
         tc_commit(pv_done(g));
       };
@@ -408,14 +408,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int g = 0; g < ngroups && ok; ++g) {
           ok = mbar_wait(p_full(g), j & 1, p.err);  // P_g(j) written (and O_g rescaled if needed)
           if (!ok) break;
-          tc_fence_after();
-          issue_pv(g, j);
           if (next) {
             ok = mbar_wait(s_empty(g), j & 1, p.err);  // S_g(j) read
             if (!ok) break;
-            tc_fence_after();
-            issue_s(g, j + 1);
           }
+          tc_fence_after();
+          if (next) issue_s(g, j + 1);
+          issue_pv(g, j);
         }
         tc_commit(kv_empty0 + 8 * (j % kAttnStages));  // K_j and V_j are no longer read
       }
@@ -425,7 +424,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if (warp >= 4 && (warp - 4) / 4 < ngroups) {
     // ------------------------------------------------------------ softmax
-    softmax_group<T>(p, tile, h, nk, (warp - 4) / 4, warp & 3, lane, tmem, smem, grp0);
+    softmax_group<T>(p, tile, h, nk, (warp - 4) / 4, warp & 3, lane, tmem, grp0);
   }
   tc_fence_before();
   __syncthreads();
