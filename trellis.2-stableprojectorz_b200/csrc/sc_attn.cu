@@ -9,37 +9,40 @@
 //
 // One CTA per (256 query rows of one sequence, head), 384 threads:
 //   warp 0     TMA producer: the two 128-row Q tiles once, then per 128-key
-//              tile the K tile and the V^T tile into a 3-slot ring
-//   warp 1     TMEM owner and single-thread MMA issuer, per key tile j:
-//              S_0(j+1) = Q_0 K_{j+1}^T, then O_0 += P_0(j) V_j, then the same
-//              for group 1, so the tensor core serves one softmax group while
-//              the other works; the next S goes first because the group waits
-//              for it, while O is needed only by a rescale and P's columns
-//              only after the next tile's row max (S: M 128, N 128, K 64;
-//              PV: M 128, N 64, K 128; accumulators in tensor memory; P V
-//              reads P, its A operand, from tensor memory and V^T from
-//              shared memory)
+//              tile the K tile and the V^T tile into a 4-slot ring
+//   warp 1     TMEM owner and single-thread MMA issuer over the steps
+//              i = j * groups + g (key tile j, query group g): S of step i
+//              = Q_g K_j^T goes into one of three 128-column S buffers shared
+//              by the groups (buffer i % 3); when group g's softmax has
+//              written P over the first 64 columns of that buffer, O_g +=
+//              P V_j reads P as its A operand from tensor memory and V^T from
+//              shared memory, and once that product is done, S of step i + 3
+//              goes into the freed buffer.  So a group usually finds its next
+//              S computed while it still works on the current tile, and the
+//              tensor core alternates between the groups (S: M 128, N 128,
+//              K 64; PV: M 128, N 64, K 128; f32 accumulators in tensor
+//              memory)
 //   warps 4-7, 8-11  softmax groups 0 and 1, one query row per thread (TMEM
 //              lane): two passes over its S row (row max, then
 //              p = 2^(s*scale*log2 e - m) and its sum), P as packed bf16/f16
-//              pairs into the group's tensor-memory columns.  The output O
+//              pairs over the S columns already read.  The output O
 //              accumulates in tensor memory across key tiles; its row max m
 //              moves only when a tile's max exceeds it by more than 2^8
 //              (conditional rescaling, the running-max trick of
 //              FlashAttention-4), and only then is the row of O rescaled
 //              in tensor memory.
-// Measured on B200 (32k tokens x 16 heads): 625 TFLOP/s; 563 with the
-// product P V issued before the next S instead of after; 540 with P staged
-// in shared memory in the 128B swizzle (eight 16-byte stores per 64 keys and
-// a proxy fence per tile instead of one tcgen05.st), 532 before the packed
-// f32x2 arithmetic of the weight loop.  Computing one in
+// Measured on B200 (32k tokens x 16 heads): 711 TFLOP/s.  Earlier layouts:
+// one S buffer per group, the next S issued right after the group's P was
+// written (before its P V) 625, after its P V 563; P staged in shared memory
+// in the 128B swizzle (eight 16-byte stores per 64 keys and a proxy fence
+// per tile instead of one tcgen05.st) 540; before the packed f32x2
+// arithmetic of the weight loop 532.  Computing one in
 // eight / four / two of the weights with a cubic 2^f polynomial on the FMA
-// pipe instead of ex2 (FlashAttention-4's offload) measured 507 / 492 / 433:
-// the softmax was then bound by instruction issue, not by the ex2 unit.
-// 64-key tiles with S double-buffered per group (S_g(j+2) issued right after
-// PV_g(j), so a group never waits for its next S) measured 428: the fixed
-// per-tile costs (barrier waits, fences, row-max tail) double, and an N = 64
-// product reads more shared memory per FLOP than N = 128.
+// pipe instead of ex2 (FlashAttention-4's offload) measured 507 / 492 / 433
+// against 540: the softmax was then bound by instruction issue, not by the
+// ex2 unit.  64-key tiles with S double-buffered per group measured 428: the
+// fixed per-tile costs (barrier waits, fences, row-max tail) double, and an
+// N = 64 product reads more shared memory per FLOP than N = 128.
 // Every operand the MMA reads is K-major: V is first transposed per head into
 // V^T [H, 64, keys], each sequence starting at a multiple of 8 keys so every
 // TMA inner coordinate is 16-byte aligned.  Key columns past the sequence end
@@ -61,7 +64,7 @@ namespace {
 
 constexpr int kAttnD = 64;          // head dim
 constexpr int kAttnTile = 128;      // query rows per softmax group and keys per step
-constexpr int kAttnStages = 3;      // K / V^T ring
+constexpr int kAttnStages = 4;      // K / V^T ring
 constexpr int kAttnThreads = 384;   // 12 warps: producer, MMA, 2 idle, 2 softmax groups of 4
 constexpr int kTileBytes = kAttnTile * kAttnD * 2;   // 16 KB: Q, K or V^T tile
 // shared-memory plan (1024-byte aligned pieces)
@@ -69,8 +72,11 @@ constexpr int kOffQ = 0;                                           // Q of group
 constexpr int kOffKV = kOffQ + 2 * kTileBytes;                     // stage s: K at +0, V^T at +16 KB
 constexpr int kOffBar = kOffKV + kAttnStages * 2 * kTileBytes;
 constexpr int kAttnSmem = kOffBar + 256 + 1024;                    // barriers + alignment slack
-// tensor memory of group g: S at [128g, 128g+128), O at [256+64g, 320+64g),
-// P (two 16-bit weights per 32-bit column) at [384+64g, 448+64g)
+// Tensor memory: a ring of three 128-column S buffers at [128b, 128b+128)
+// shared by the two groups (S of step i = j * groups + g in buffer i % 3; the
+// softmax overwrites the first 64 columns with P, two 16-bit weights per
+// 32-bit column), and O of group g at [384+64g, 448+64g).
+constexpr int kSBufs = 3;
 constexpr uint32_t kTmemCols = 512;
 // Conditional rescaling: the running row max used for the exponentials moves
 // only when a tile's max exceeds it by more than 2^8, so most tiles leave the
@@ -178,17 +184,19 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
 // One softmax group (four warps, one query row per thread = TMEM lane):
 // for every key tile, the row max of S (two 64-column reads), conditional
 // rescaling of the output accumulator O in tensor memory, the weights
-// p = 2^(s * scale * log2 e - m) as bf16/f16 pairs into the group's P
-// columns of tensor memory (lane = query row, the A operand layout of the
-// second product), and the running sum; at the end O / sum to global memory.
+// p = 2^(s * scale * log2 e - m) as bf16/f16 pairs written over the first
+// 64 columns of the same S buffer (lane = query row, the A operand layout of
+// the second product), and the running sum; at the end O / sum to global
+// memory.  s_full0 / p_full0: the three S buffers' barriers; o_done: this
+// group's "P V done" barrier.
 template <typename T>
 __device__ __forceinline__ void softmax_group(const AttnParams& p, const AttnTile& tile, int h, int nk, int g,
-                                              int quad, int lane, uint32_t tmem, uint32_t grp0) {
-  const uint32_t s_full = grp0 + 32u * g, s_empty = s_full + 8, p_full = s_full + 16, pv_done = s_full + 24;
+                                              int ng, int quad, int lane, uint32_t tmem, uint32_t s_full0,
+                                              uint32_t p_full0, uint32_t o_done) {
   const int row = quad * 32 + lane;
   const int qrow = tile.q0 + g * kAttnTile + row;
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-  const uint32_t sa = lane_base + g * 128, oa = lane_base + 256 + g * 64;
+  const uint32_t oa = lane_base + 384u + g * 64;
   float m = -INFINITY, l = 0.f;
   bool ok = true;
   auto wait_warp = [&](uint32_t bar, uint32_t parity) -> bool {
@@ -199,7 +207,10 @@ __device__ __forceinline__ void softmax_group(const AttnParams& p, const AttnTil
   for (int j = 0; j < nk; ++j) {
     const int valid = min(kAttnTile, tile.k1 - (tile.k0 + j * kAttnTile));  // key columns in the sequence
     const bool full = valid == kAttnTile;                                    // warp-uniform
-    if (!wait_warp(s_full, j & 1)) {
+    const int step = j * ng + g;
+    const uint32_t b = static_cast<uint32_t>(step % kSBufs), use = static_cast<uint32_t>(step / kSBufs);
+    const uint32_t sa = lane_base + 128u * b;
+    if (!wait_warp(s_full0 + 8u * b, use & 1u)) {
       ok = false;
       break;
     }
@@ -226,25 +237,25 @@ __device__ __forceinline__ void softmax_group(const AttnParams& p, const AttnTil
     const bool move = m_tile > m + kRescaleLog2;  // always true on the first tile (m = -inf)
     const float m_new = move ? m_tile : m;
     const float alpha = move ? ex2_ftz(m - m_new) : 1.f;
-    // P_g(j-1) has been multiplied and O_g updated before P's columns and O are touched
-    if (j > 0) {
-      if (!wait_warp(pv_done, (j - 1) & 1)) {
+    // A rescale waits for O_g to hold the sum through tile j-1.  The S
+    // buffer itself was free when S_g(j) was issued into it (the product that
+    // last read its P was done), and P_g(j) goes there.
+    if (j > 0 && __any_sync(0xffffffffu, move)) {
+      if (!wait_warp(o_done, (j - 1) & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if (__any_sync(0xffffffffu, move)) {
-        float o[64];
-        tmem_ld64(oa, o);
-        uint32_t w[32];
+      float o[64];
+      tmem_ld64(oa, o);
+      uint32_t w[32];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
+      for (int half = 0; half < 2; ++half) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[half * 32 + i] * alpha);
-          tmem_st32(oa + half * 32, w);
-        }
-        tmem_wait_st();
+        for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(o[half * 32 + i] * alpha);
+        tmem_st32(oa + half * 32, w);
       }
+      tmem_wait_st();
     }
     unsigned long long sumv[4];  // pairs of partial sums
 #pragma unroll
@@ -268,12 +279,13 @@ __device__ __forceinline__ void softmax_group(const AttnParams& p, const AttnTil
         sumv[(i >> 1) & 3] = add_f2(sumv[(i >> 1) & 3], pp);
         pk[i / 2] = pack2<T>(p0, p1);
       }
-      tmem_st32(lane_base + 384u + g * 64 + 32u * c, pk);  // keys 64c .. 64c+63
+      // keys 64c .. 64c+63 into columns 32c .. 32c+31, all of them S columns
+      // this thread has already read
+      tmem_st32(sa + 32u * c, pk);
     }
     tmem_wait_st();
     tc_fence_before();
-    mbar_arrive(s_empty);        // S_g(j) is read
-    mbar_arrive(p_full);         // P_g(j) and the O rescale (tcgen05.st) are complete
+    mbar_arrive(p_full0 + 8u * b);  // P_g(j) and the O rescale (tcgen05.st) are complete
     const unsigned long long s2 = add_f2(add_f2(sumv[0], sumv[1]), add_f2(sumv[2], sumv[3]));
     float sa2, sb2;
     f2_split(s2, sa2, sb2);
@@ -283,7 +295,7 @@ __device__ __forceinline__ void softmax_group(const AttnParams& p, const AttnTil
   }
   float o[64];
   bool have = false;
-  if (ok && nk > 0 && wait_warp(pv_done, (nk - 1) & 1)) {
+  if (ok && nk > 0 && wait_warp(o_done, (nk - 1) & 1)) {
     tc_fence_after();
     tmem_ld64(oa, o);
     have = true;
@@ -312,15 +324,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 24);
   const uint32_t bar0 = smem_u32(bars);
-  // barriers: q_full, kv_full[3], kv_empty[3], then per group g: s_full, s_empty, p_full, pv_done
+  // barriers: q_full, kv_full[4], kv_empty[4], s_full[3] and p_full[3] (one
+  // per S buffer), o_done[2] (one per group: its P V products done), done
   const uint32_t q_full = bar0;
-  const uint32_t kv_full0 = bar0 + 8, kv_empty0 = bar0 + 8 * (1 + kAttnStages);
-  const uint32_t grp0 = bar0 + 8 * (1 + 2 * kAttnStages);  // group g's four barriers at grp0 + 32g
-  const uint32_t done_bar = grp0 + 64;
-  auto s_full = [&](int g) { return grp0 + 32u * g; };
-  auto s_empty = [&](int g) { return grp0 + 32u * g + 8; };
-  auto p_full = [&](int g) { return grp0 + 32u * g + 16; };
-  auto pv_done = [&](int g) { return grp0 + 32u * g + 24; };
+  const uint32_t kv_full0 = bar0 + 8, kv_empty0 = kv_full0 + 8 * kAttnStages;
+  const uint32_t s_full0 = kv_empty0 + 8 * kAttnStages, p_full0 = s_full0 + 8 * kSBufs;
+  const uint32_t o_done0 = p_full0 + 8 * kSBufs, done_bar = o_done0 + 16;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const AttnTile tile = p.tiles[blockIdx.x];
   const int h = blockIdx.y;
@@ -333,12 +342,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(kv_full0 + 8 * st, 1);
       mbar_init(kv_empty0 + 8 * st, 1);
     }
-    for (int g = 0; g < 2; ++g) {
-      mbar_init(s_full(g), 1);
-      mbar_init(s_empty(g), 128);
-      mbar_init(p_full(g), 128);
-      mbar_init(pv_done(g), 1);
+    for (int sb = 0; sb < kSBufs; ++sb) {
+      mbar_init(s_full0 + 8 * sb, 1);
+      mbar_init(p_full0 + 8 * sb, 128);
     }
+    mbar_init(o_done0, 1);
+    mbar_init(o_done0 + 8, 1);
     mbar_init(done_bar, 1);
     fence_mbar_init();
   }
@@ -373,50 +382,61 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    // Per key tile j: S_0(j+1), PV_0(j), S_1(j+1), PV_1(j): while one group
-    // runs its softmax the tensor core works for the other.
+    // Steps i = j * groups + g in order: P V of step i as soon as its P is
+    // written, then S of step i + 3 into the buffer that step i's P occupied
+    // once that product is done (S of the first three steps up front).  A
+    // group thus usually finds its next S computed while it still works on
+    // the current tile, and the tensor core alternates between the groups.
     if (lane == 0 && nk > 0) {
       const bool bf16 = std::is_same_v<T, __nv_bfloat16>;
       const uint32_t id_s = idesc_f16(128, 128, bf16), id_u = idesc_f16(128, 64, bf16);
-      auto issue_s = [&](int g, int j) {  // S_g(j) = Q_g K_j^T; K_j landed and S_g(j-1) was read
+      auto issue_s = [&](int step) {  // S of step into buffer step % 3; its K landed, the buffer is free
+        const int g = step % ngroups, j = step / ngroups, sb = step % kSBufs;
         const uint32_t kb = sbase + kOffKV + (j % kAttnStages) * 2 * kTileBytes;
         const uint32_t qb = sbase + kOffQ + g * kTileBytes;
 #pragma unroll
         for (int k = 0; k < kAttnD / 16; ++k)
-          tc_mma_f16(tmem + g * 128, smem_desc(qb + 32u * k, 1024, 2), smem_desc(kb + 32u * k, 1024, 2), id_s,
+          tc_mma_f16(tmem + 128u * sb, smem_desc(qb + 32u * k, 1024, 2), smem_desc(kb + 32u * k, 1024, 2), id_s,
                      k > 0 ? 1u : 0u);
-        tc_commit(s_full(g));
+        tc_commit(s_full0 + 8u * sb);
       };
-      auto issue_pv = [&](int g, int j) {  // O_g (+)= P_g(j) V_j
+      auto issue_pv = [&](int step) {  // O_g (+)= P V_j, P in the first 64 columns of buffer step % 3
+        const int g = step % ngroups, j = step / ngroups, sb = step % kSBufs;
         const uint32_t vb = sbase + kOffKV + (j % kAttnStages) * 2 * kTileBytes + kTileBytes;
 #pragma unroll
         for (int k = 0; k < kAttnTile / 16; ++k) {
           const uint32_t atom = static_cast<uint32_t>(k >> 2), off = 32u * (k & 3);
-          tc_mma_f16_tmem_a(tmem + 256 + g * 64, tmem + 384u + g * 64 + 8u * k,
+          tc_mma_f16_tmem_a(tmem + 384u + g * 64, tmem + 128u * sb + 8u * k,
                             smem_desc(vb + atom * (kTileBytes / 2) + off, 1024, 2), id_u, (j > 0 || k > 0) ? 1u : 0u);
         }
-        tc_commit(pv_done(g));
+        tc_commit(o_done0 + 8u * g);
       };
-      bool ok = mbar_wait(q_full, 0, p.err) && mbar_wait(kv_full0, 0, p.err);
-      if (ok) {
+      auto k_landed = [&](int j) {
+        return mbar_wait(kv_full0 + 8 * (j % kAttnStages), (j / kAttnStages) & 1, p.err);
+      };
+      const int total = nk * ngroups;
+      bool ok = mbar_wait(q_full, 0, p.err);
+      for (int i = 0; ok && i < kSBufs && i < total; ++i) {
+        if (i % ngroups == 0) ok = k_landed(i / ngroups);
+        if (!ok) break;
         tc_fence_after();
-        for (int g = 0; g < ngroups; ++g) issue_s(g, 0);
+        issue_s(i);
       }
-      for (int j = 0; ok && j < nk; ++j) {
-        const bool next = j + 1 < nk;
-        if (next && !mbar_wait(kv_full0 + 8 * ((j + 1) % kAttnStages), ((j + 1) / kAttnStages) & 1, p.err)) break;
-        for (int g = 0; g < ngroups && ok; ++g) {
-          ok = mbar_wait(p_full(g), j & 1, p.err);  // P_g(j) written (and O_g rescaled if needed)
+      for (int i = 0; ok && i < total; ++i) {
+        const int g = i % ngroups, j = i / ngroups;
+        ok = mbar_wait(p_full0 + 8u * (i % kSBufs), (i / kSBufs) & 1, p.err);  // P of step i written
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(i);
+        if (g == ngroups - 1) tc_commit(kv_empty0 + 8 * (j % kAttnStages));  // K_j and V_j are no longer read
+        const int i3 = i + kSBufs;
+        if (i3 < total) {
+          if (i3 % ngroups == 0) ok = k_landed(i3 / ngroups);
+          ok = ok && mbar_wait(o_done0 + 8u * g, j & 1, p.err);  // P V of step i done: its buffer is free
           if (!ok) break;
-          if (next) {
-            ok = mbar_wait(s_empty(g), j & 1, p.err);  // S_g(j) read
-            if (!ok) break;
-          }
           tc_fence_after();
-          if (next) issue_s(g, j + 1);
-          issue_pv(g, j);
+          issue_s(i3);
         }
-        tc_commit(kv_empty0 + 8 * (j % kAttnStages));  // K_j and V_j are no longer read
       }
       // every MMA issued must finish before TMEM is released
       tc_commit(done_bar);
@@ -424,7 +444,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if (warp >= 4 && (warp - 4) / 4 < ngroups) {
     // ------------------------------------------------------------ softmax
-    softmax_group<T>(p, tile, h, nk, (warp - 4) / 4, warp & 3, lane, tmem, grp0);
+    const int g = (warp - 4) / 4;
+    softmax_group<T>(p, tile, h, nk, g, ngroups, warp & 3, lane, tmem, s_full0, p_full0, o_done0 + 8u * g);
   }
   tc_fence_before();
   __syncthreads();
