@@ -36,11 +36,12 @@
 // written (before its P V) 625, after its P V 563; P staged in shared memory
 // in the 128B swizzle (eight 16-byte stores per 64 keys and a proxy fence
 // per tile instead of one tcgen05.st) 540; before the packed f32x2
-// arithmetic of the weight loop 532.  Computing one in
-// eight / four / two of the weights with a cubic 2^f polynomial on the FMA
-// pipe instead of ex2 (FlashAttention-4's offload) measured 507 / 492 / 433
-// against 540: the softmax was then bound by instruction issue, not by the
-// ex2 unit.  64-key tiles with S double-buffered per group measured 428: the
+// arithmetic of the weight loop 532.  Computing one in eight / four of the
+// weights with a cubic 2^f polynomial on the FMA pipe instead of ex2
+// (FlashAttention-4's offload; packed f32x2, fitted to 7.5e-5 relative
+// error) measured 637 / 564 against 711 with this layout (507 / 492 against
+// 540 with the first): the softmax is bound by its instruction stream, not
+// by the ex2 unit.  64-key tiles with S double-buffered per group measured 428: the
 // fixed per-tile costs (barrier waits, fences, row-max tail) double, and an
 // N = 64 product reads more shared memory per FLOP than N = 128.
 // Every operand the MMA reads is K-major: V is first transposed per head into
