@@ -43,7 +43,10 @@
 // 540 with the first): the softmax is bound by its instruction stream, not
 // by the ex2 unit.  64-key tiles with S double-buffered per group measured 428: the
 // fixed per-tile costs (barrier waits, fences, row-max tail) double, and an
-// N = 64 product reads more shared memory per FLOP than N = 128.
+// N = 64 product reads more shared memory per FLOP than N = 128.  Keeping
+// keys 64..127 of S in registers from the row-max pass to the weight pass
+// (one TMEM read fewer per tile, their P at columns 64..95): 698-720, no
+// change.
 // Every operand the MMA reads is K-major: V is first transposed per head into
 // V^T [H, 64, keys], each sequence starting at a multiple of 8 keys so every
 // TMA inner coordinate is 16-byte aligned.  Key columns past the sequence end
