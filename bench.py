@@ -1223,7 +1223,7 @@ def run_attn(args):
     bf16_peak = float(peaks["bf16_tflops"])
     roof = {"bound": "tensor", "kernel": "k_attn_fwd<bf16>", "achieved": flops / step_s / 1e12, "peak": bf16_peak,
             "unit": "TFLOP/s", "frac": flops / step_s / 1e12 / bf16_peak,
-            "flops_per_call": flops, "units": "4 * sum(len^2) * heads * 64 (QK^T and PV), V^T pass included",
+            "flops_per_call": flops, "units": "4 * sum(len^2) * heads * 64 (QK^T and PV), the whole call timed",
             "traffic": None, "peak_source": f"{peak_src} bf16_tflops (burst)"}
     # end to end: H2D of q, k, v from pinned memory, attention, D2H of the output
     pin = [t.pin_memory() for t in host]

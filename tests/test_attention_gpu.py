@@ -100,3 +100,16 @@ def test_refuses_bad_arguments(pkg, cuda):
         pkg.sparse_attention(q32, q32, q32, [0, 10])
     with pytest.raises(TypeError):
         pkg.sparse_attention(q.float(), k.float(), v.float(), [0, 10])
+
+
+def test_sequences_stay_isolated(pkg, oracle, cuda):
+    """The last key tile of a sequence also covers rows of the next one; a
+    NaN in the next sequence's K or V must not reach this sequence's output."""
+    cu = np.array([0, 200, 500], np.int32)
+    q, k, v = _qkv(cuda, 500, 500, 2, torch.bfloat16, 12)
+    k[250] = float("nan")  # rows 200..255 share sequence 0's second key tile
+    v[230] = float("nan")
+    out = pkg.sparse_attention(q, k, v, cu)
+    ref = oracle.attention_varlen(_f64(q[:200]), _f64(k[:200]), _f64(v[:200]), [0, 200])
+    assert torch.isfinite(out[:200]).all()
+    assert rel_l2(_f64(out[:200]), ref) < TOL

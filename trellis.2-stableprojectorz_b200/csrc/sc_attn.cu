@@ -9,14 +9,14 @@
 //
 // One CTA per (256 query rows of one sequence, head), 384 threads:
 //   warp 0     TMA producer: the two 128-row Q tiles once, then per 128-key
-//              tile the K tile and the V^T tile into a 4-slot ring
+//              tile the K tile and the V tile into a 4-slot ring
 //   warp 1     TMEM owner and single-thread MMA issuer over the steps
 //              i = j * groups + g (key tile j, query group g): S of step i
 //              = Q_g K_j^T goes into one of three 128-column S buffers shared
 //              by the groups (buffer i % 3); when group g's softmax has
 //              written P over the first 64 columns of that buffer, O_g +=
-//              P V_j reads P as its A operand from tensor memory and V^T from
-//              shared memory, and once that product is done, S of step i + 3
+//              P V_j reads P as its A operand from tensor memory and V from
+//              shared memory (MN-major), and once that product is done, S of step i + 3
 //              goes into the freed buffer.  So a group usually finds its next
 //              S computed while it still works on the current tile, and the
 //              tensor core alternates between the groups (S: M 128, N 128,
@@ -31,7 +31,9 @@
 //              (conditional rescaling, the running-max trick of
 //              FlashAttention-4), and only then is the row of O rescaled
 //              in tensor memory.
-// Measured on B200 (32k tokens x 16 heads): 711 TFLOP/s.  Earlier layouts:
+// Measured on B200 (32k tokens x 16 heads): 691-708 TFLOP/s (711 with V
+// transposed first, see below; the 10,000 + 6,384-token call gains more from
+// dropping that pass, 0.99 -> 0.958 ms).  Earlier layouts:
 // one S buffer per group, the next S issued right after the group's P was
 // written (before its P V) 625, after its P V 563; P staged in shared memory
 // in the 128B swizzle (eight 16-byte stores per 64 keys and a proxy fence
@@ -47,10 +49,13 @@
 // keys 64..127 of S in registers from the row-max pass to the weight pass
 // (one TMEM read fewer per tile, their P at columns 64..95): 698-720, no
 // change.
-// Every operand the MMA reads is K-major: V is first transposed per head into
-// V^T [H, 64, keys], each sequence starting at a multiple of 8 keys so every
-// TMA inner coordinate is 16-byte aligned.  Key columns past the sequence end
-// get p = 0.  Every mbarrier wait is bounded (SC_ETIMEOUT).
+// Q, K and V are read where they lie, [tokens, H, 64], by 3-D TMA boxes of
+// 128 rows of one head; Q and K are K-major operands, V an MN-major one.  An
+// earlier build transposed V per head into a K-major V^T first: a separate
+// 27 us pass and a buffer the size of V on the 16k-token call, and its
+// kernel ran 1-3% faster on a single 32k sequence.  Key columns past the
+// sequence end get p = 0, and warp 2 zeroes their V rows in shared memory.
+// Every mbarrier wait is bounded (SC_ETIMEOUT).
 #include "sc_common.cuh"
 #include "sc_internal.h"
 
@@ -68,12 +73,12 @@ namespace {
 
 constexpr int kAttnD = 64;          // head dim
 constexpr int kAttnTile = 128;      // query rows per softmax group and keys per step
-constexpr int kAttnStages = 4;      // K / V^T ring
+constexpr int kAttnStages = 4;      // K / V ring
 constexpr int kAttnThreads = 384;   // 12 warps: producer, MMA, 2 idle, 2 softmax groups of 4
-constexpr int kTileBytes = kAttnTile * kAttnD * 2;   // 16 KB: Q, K or V^T tile
+constexpr int kTileBytes = kAttnTile * kAttnD * 2;   // 16 KB: Q, K or V tile
 // shared-memory plan (1024-byte aligned pieces)
 constexpr int kOffQ = 0;                                           // Q of group 0, group 1 at +16 KB
-constexpr int kOffKV = kOffQ + 2 * kTileBytes;                     // stage s: K at +0, V^T at +16 KB
+constexpr int kOffKV = kOffQ + 2 * kTileBytes;                     // stage s: K at +0, V at +16 KB
 constexpr int kOffBar = kOffKV + kAttnStages * 2 * kTileBytes;
 constexpr int kAttnSmem = kOffBar + 256 + 1024;                    // barriers + alignment slack
 // Tensor memory: a ring of three 128-column S buffers at [128b, 128b+128)
@@ -92,8 +97,7 @@ constexpr float kRescaleLog2 = 8.f;
 struct AttnTile {
   int32_t q0, q1;      // query rows [q0, min(q0 + 256, q1))
   int32_t k0, k1;      // key rows [k0, k1)
-  int32_t kp;          // column of key k0 in V^T (a multiple of 8)
-  int32_t pad;
+  int32_t pad0, pad1;
 };
 
 struct AttnParams {
@@ -321,7 +325,7 @@ __device__ __forceinline__ void softmax_group(const AttnParams& p, const AttnTil
 template <typename T>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     k_attn_fwd(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-               const __grid_constant__ CUtensorMap tmVt, const AttnParams p) {
+               const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -334,11 +338,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t kv_full0 = bar0 + 8, kv_empty0 = kv_full0 + 8 * kAttnStages;
   const uint32_t s_full0 = kv_empty0 + 8 * kAttnStages, p_full0 = s_full0 + 8 * kSBufs;
   const uint32_t o_done0 = p_full0 + 8 * kSBufs, done_bar = o_done0 + 16;
+  // the last key tile's V landed (MMA -> warp 2) / its rows past the
+  // sequence end are zeroed (warp 2 -> MMA)
+  const uint32_t v_req = done_bar + 8, v_fixed = done_bar + 16;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const AttnTile tile = p.tiles[blockIdx.x];
   const int h = blockIdx.y;
   const int nk = (tile.k1 - tile.k0 + kAttnTile - 1) / kAttnTile;  // key tiles (0: empty key sequence)
   const int ngroups = tile.q0 + kAttnTile < tile.q1 ? 2 : 1;       // the second group may have no rows
+  const bool last_partial = nk > 0 && tile.k1 - tile.k0 < nk * kAttnTile;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -353,6 +361,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(o_done0, 1);
     mbar_init(o_done0 + 8, 1);
     mbar_init(done_bar, 1);
+    mbar_init(v_req, 1);
+    mbar_init(v_fixed, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -369,7 +379,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (lane == 0 && nk > 0) {
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
-      prefetch_tmap(&tmVt);
+      prefetch_tmap(&tmV);
       mbar_arrive_expect_tx(q_full, ngroups * kTileBytes);
       for (int g = 0; g < ngroups; ++g)
         tma_load_3d(sbase + kOffQ + g * kTileBytes, &tmQ, 0, h, tile.q0 + g * kAttnTile, q_full);
@@ -379,9 +389,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t kb = sbase + kOffKV + st * 2 * kTileBytes;
         mbar_arrive_expect_tx(kv_full0 + 8 * st, 2 * kTileBytes);
         tma_load_3d(kb, &tmK, 0, h, tile.k0 + j * kAttnTile, kv_full0 + 8 * st);
-        // V^T: two 64-key atoms of [64 dims][64 keys]
-        tma_load_3d(kb + kTileBytes, &tmVt, tile.kp + j * kAttnTile, 0, h, kv_full0 + 8 * st);
-        tma_load_3d(kb + kTileBytes + kTileBytes / 2, &tmVt, tile.kp + j * kAttnTile + 64, 0, h, kv_full0 + 8 * st);
+        // V as stored: [128 keys][64 dims], read by the MMA as an MN-major operand
+        tma_load_3d(kb + kTileBytes, &tmV, 0, h, tile.k0 + j * kAttnTile, kv_full0 + 8 * st);
       }
     }
   } else if (warp == 1) {
@@ -393,7 +402,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // the current tile, and the tensor core alternates between the groups.
     if (lane == 0 && nk > 0) {
       const bool bf16 = std::is_same_v<T, __nv_bfloat16>;
-      const uint32_t id_s = idesc_f16(128, 128, bf16), id_u = idesc_f16(128, 64, bf16);
+      // P V takes V MN-major (bit 16 of the instruction descriptor): the tile
+      // as TMA lands it, key rows of 64 dims in the 128-byte swizzle
+      const uint32_t id_s = idesc_f16(128, 128, bf16), id_u = idesc_f16(128, 64, bf16) | (1u << 16);
       auto issue_s = [&](int step) {  // S of step into buffer step % 3; its K landed, the buffer is free
         const int g = step % ngroups, j = step / ngroups, sb = step % kSBufs;
         const uint32_t kb = sbase + kOffKV + (j % kAttnStages) * 2 * kTileBytes;
@@ -407,16 +418,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       auto issue_pv = [&](int step) {  // O_g (+)= P V_j, P in the first 64 columns of buffer step % 3
         const int g = step % ngroups, j = step / ngroups, sb = step % kSBufs;
         const uint32_t vb = sbase + kOffKV + (j % kAttnStages) * 2 * kTileBytes + kTileBytes;
+        // MN-major, 128B swizzle: one 64-element atom along N, 8-key groups
+        // 1024 bytes apart along K; step k starts at key 16k
 #pragma unroll
-        for (int k = 0; k < kAttnTile / 16; ++k) {
-          const uint32_t atom = static_cast<uint32_t>(k >> 2), off = 32u * (k & 3);
-          tc_mma_f16_tmem_a(tmem + 384u + g * 64, tmem + 128u * sb + 8u * k,
-                            smem_desc(vb + atom * (kTileBytes / 2) + off, 1024, 2), id_u, (j > 0 || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < kAttnTile / 16; ++k)
+          tc_mma_f16_tmem_a(tmem + 384u + g * 64, tmem + 128u * sb + 8u * k, smem_desc(vb + 2048u * k, 1024, 2),
+                            id_u, (j > 0 || k > 0) ? 1u : 0u);
         tc_commit(o_done0 + 8u * g);
       };
       auto k_landed = [&](int j) {
-        return mbar_wait(kv_full0 + 8 * (j % kAttnStages), (j / kAttnStages) & 1, p.err);
+        const bool r = mbar_wait(kv_full0 + 8 * (j % kAttnStages), (j / kAttnStages) & 1, p.err);
+        if (r && j == nk - 1 && last_partial) mbar_arrive(v_req);  // warp 2 may clear its V tail
+        return r;
       };
       const int total = nk * ngroups;
       bool ok = mbar_wait(q_full, 0, p.err);
@@ -431,6 +444,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ok = mbar_wait(p_full0 + 8u * (i % kSBufs), (i / kSBufs) & 1, p.err);  // P of step i written
         if (!ok) break;
         tc_fence_after();
+        if (g == 0 && j == nk - 1 && last_partial) {
+          ok = mbar_wait(v_fixed, 0, p.err);  // warp 2 cleared the V rows past the sequence end
+          if (!ok) break;
+          tc_fence_after();
+        }
         issue_pv(i);
         if (g == ngroups - 1) tc_commit(kv_empty0 + 8 * (j % kAttnStages));  // K_j and V_j are no longer read
         const int i3 = i + kSBufs;
@@ -446,6 +464,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_commit(done_bar);
       mbar_wait(done_bar, 0, p.err);
     }
+  } else if (warp == 2) {
+    // ------------------------------------------------- V tail of the last tile
+    // The last key tile of a sequence also holds rows of the next sequence
+    // (or TMA zero fill) past its end.  Their weights are 0, but 0 * NaN is
+    // NaN: those V rows are zeroed in shared memory before the tile's first
+    // P V, so one sequence's values never reach another's output (K rows
+    // there are harmless: their scores are masked).
+    if (last_partial) {
+      int w = 1;
+      if (lane == 0) w = mbar_wait(v_req, 0, p.err) ? 1 : 0;
+      if (__shfl_sync(0xffffffffu, w, 0) != 0) {
+        const int valid = tile.k1 - (tile.k0 + (nk - 1) * kAttnTile);
+        const uint32_t vb = sbase + kOffKV + ((nk - 1) % kAttnStages) * 2 * kTileBytes + kTileBytes;
+        for (uint32_t a = vb + 128u * valid + 16u * lane; a < vb + kTileBytes; a += 512u)
+          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
+        fence_proxy_async_smem();  // the generic stores before the MMA's async-proxy reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(v_fixed);
+      }
+    }
   } else if (warp >= 4 && (warp - 4) / 4 < ngroups) {
     // ------------------------------------------------------------ softmax
     const int g = (warp - 4) / 4;
@@ -459,91 +497,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 }
 
-// V [tokens, H, 64] -> V^T [H, 64, cols]: token t of sequence b goes to
-// column kp[b] + (t - k0[b]).  One block per (64-token chunk, head); rows of
-// the chunk that belong to different sequences are placed independently.
-template <typename T>
-__global__ void __launch_bounds__(256) k_attn_vt(const T* __restrict__ v, const int32_t* __restrict__ col_of_token,
-                                                 int64_t tokens, int heads, int64_t cols, T* __restrict__ vt) {
-  __shared__ T tile[64][kAttnD + 8];
-  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * 64;
-  const int h = blockIdx.y;
-  // load 64 tokens x 64 dims (8 threads per token row, 16 bytes each)
-  for (int e = threadIdx.x; e < 64 * 8; e += blockDim.x) {
-    const int r = e >> 3, c = e & 7;
-    const int64_t t = t0 + r;
-    uint4 val = make_uint4(0u, 0u, 0u, 0u);
-    if (t < tokens) val = __ldg(reinterpret_cast<const uint4*>(v + (t * heads + h) * kAttnD) + c);
-    const T* pv = reinterpret_cast<const T*>(&val);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) tile[r][c * 8 + k] = pv[k];
-  }
-  __syncthreads();
-  // write dim-major: thread (d, r) writes V^T[h][d][col(t0 + r)]
-  for (int e = threadIdx.x; e < 64 * kAttnD; e += blockDim.x) {
-    const int d = e >> 6, r = e & 63;
-    const int64_t t = t0 + r;
-    if (t < tokens) vt[(static_cast<int64_t>(h) * kAttnD + d) * cols + __ldg(col_of_token + t)] = tile[r][d];
-  }
-}
-
 template <typename T>
 sc_status launch_attn(Handle* h, const void* q, const void* k, const void* v, void* out, const int32_t* cu_q,
                       const int32_t* cu_kv, int batch, int heads, float scale) {
   const bool bf16 = std::is_same_v<T, __nv_bfloat16>;
   const int64_t nq = cu_q[batch], nkv = cu_kv[batch];
-  // host plan: query tiles, padded V^T columns per sequence, column of every key token
+  // host plan: one tile per 256 query rows of a sequence
   std::vector<AttnTile> tiles;
-  std::vector<int32_t> col(static_cast<size_t>(std::max<int64_t>(nkv, 1)));
-  int64_t cols = 0;
-  for (int b = 0; b < batch; ++b) {
-    const int32_t kp = static_cast<int32_t>(cols);
-    for (int64_t t = cu_kv[b]; t < cu_kv[b + 1]; ++t) col[t] = static_cast<int32_t>(kp + (t - cu_kv[b]));
-    cols += ((cu_kv[b + 1] - cu_kv[b]) + 7) / 8 * 8;
+  for (int b = 0; b < batch; ++b)
     for (int32_t q0 = cu_q[b]; q0 < cu_q[b + 1]; q0 += 2 * kAttnTile)
-      tiles.push_back(AttnTile{q0, cu_q[b + 1], cu_kv[b], cu_kv[b + 1], kp, 0});
-  }
+      tiles.push_back(AttnTile{q0, cu_q[b + 1], cu_kv[b], cu_kv[b + 1], 0, 0});
   if (tiles.empty()) return SC_OK;
-  if (cols >= (1ll << 31)) return set_error(h, SC_EINVAL, "attention: too many key tokens");
-  cols = std::max<int64_t>(cols, 8);
   const size_t tile_bytes = sizeof(AttnTile) * tiles.size();
-  const size_t col_bytes = sizeof(int32_t) * col.size();
-  const size_t vt_bytes = sizeof(T) * static_cast<size_t>(heads) * kAttnD * static_cast<size_t>(cols);
-  uint8_t* buf = nullptr;
-  const size_t off_col = (tile_bytes + 255) / 256 * 256, off_vt = off_col + (col_bytes + 255) / 256 * 256;
-  cudaError_t e = dev_alloc(h, reinterpret_cast<void**>(&buf), off_vt + vt_bytes);
-  if (e != cudaSuccess) return cuda_error(h, e, "attention buffers");
+  AttnTile* d_tiles = nullptr;
+  cudaError_t e = dev_alloc(h, reinterpret_cast<void**>(&d_tiles), tile_bytes);
+  if (e != cudaSuccess) return cuda_error(h, e, "attention plan buffer");
   auto fail = [&](cudaError_t err, const char* what) {
-    dev_free(h, buf);
+    dev_free(h, d_tiles);
     return cuda_error(h, err, what);
   };
-  AttnTile* d_tiles = reinterpret_cast<AttnTile*>(buf);
-  int32_t* d_col = reinterpret_cast<int32_t*>(buf + off_col);
-  T* vt = reinterpret_cast<T*>(buf + off_vt);
   e = cudaMemcpyAsync(d_tiles, tiles.data(), tile_bytes, cudaMemcpyHostToDevice, h->stream);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(d_col, col.data(), col_bytes, cudaMemcpyHostToDevice, h->stream);
-  // padding columns between sequences must be finite: they meet p = 0
-  if (e == cudaSuccess) e = cudaMemsetAsync(vt, 0, vt_bytes, h->stream);
   if (e != cudaSuccess) return fail(e, "attention plan copy");
-  if (nkv > 0) {
-    ++h->launches;
-    k_attn_vt<T><<<dim3(static_cast<unsigned>((nkv + 63) / 64), heads), 256, 0, h->stream>>>(
-        static_cast<const T*>(v), d_col, nkv, heads, cols, vt);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return fail(e, "attention V transpose launch");
-  }
+  // Q, K and V as given: [tokens, H, 64], boxes of 128 rows of one head
   CUtensorMap tq, tk, tv;
   const uint64_t row = static_cast<uint64_t>(heads) * kAttnD * 2;
   const uint64_t dq[3] = {kAttnD, static_cast<uint64_t>(heads), static_cast<uint64_t>(std::max<int64_t>(nq, 1))};
   const uint64_t dk[3] = {kAttnD, static_cast<uint64_t>(heads), static_cast<uint64_t>(std::max<int64_t>(nkv, 1))};
   const uint64_t sq[2] = {kAttnD * 2, row};
   const uint32_t bq[3] = {kAttnD, 1, kAttnTile};
-  const uint64_t dv[3] = {static_cast<uint64_t>(cols), kAttnD, static_cast<uint64_t>(heads)};
-  const uint64_t sv[2] = {static_cast<uint64_t>(cols) * 2, static_cast<uint64_t>(cols) * 2 * kAttnD};
-  const uint32_t bv[3] = {64, kAttnD, 1};
   if (!make_map_3d(&tq, bf16, q, dq, sq, bq) || !make_map_3d(&tk, bf16, k, dk, sq, bq) ||
-      !make_map_3d(&tv, bf16, vt, dv, sv, bv)) {
-    dev_free(h, buf);
+      !make_map_3d(&tv, bf16, v, dk, sq, bq)) {
+    dev_free(h, d_tiles);
     return set_error(h, SC_ECUDA, "cuTensorMapEncodeTiled failed (attention)");
   }
   AttnParams ap{};
@@ -558,7 +542,7 @@ sc_status launch_attn(Handle* h, const void* q, const void* k, const void* v, vo
   k_attn_fwd<T><<<dim3(static_cast<unsigned>(tiles.size()), heads), kAttnThreads, kAttnSmem, h->stream>>>(tq, tk, tv,
                                                                                                          ap);
   e = cudaGetLastError();
-  dev_free(h, buf);  // stream-ordered: released after the kernels that use it
+  dev_free(h, d_tiles);  // stream-ordered: released after the kernel that uses it
   return e == cudaSuccess ? SC_OK : cuda_error(h, e, "attention launch");
 }
 
