@@ -48,7 +48,11 @@
 // N = 64 product reads more shared memory per FLOP than N = 128.  Keeping
 // keys 64..127 of S in registers from the row-max pass to the weight pass
 // (one TMEM read fewer per tile, their P at columns 64..95): 698-720, no
-// change.
+// change.  Two threads per query row (eight softmax warps per group, each
+// warp on 64 of a tile's 128 keys, the half-row maxima exchanged through
+// shared memory under a named barrier per tile): 596 against 691, and the
+// 16k-token call 1.087 against 0.956 ms -- the per-tile exchange and
+// barrier cost more than the extra warps hide.
 // Q, K and V are read where they lie, [tokens, H, 64], by 3-D TMA boxes of
 // 128 rows of one head; Q and K are K-major operands, V an MN-major one.  An
 // earlier build transposed V per head into a K-major V^T first: a separate
