@@ -27,7 +27,7 @@ constexpr int kDwRows = 32;      // rows per block (a quarter tile)
 constexpr int kDwChans = 64;     // channels per block
 constexpr int kDwVec = 8;        // channels per thread
 constexpr int kDwThreads = kDwRows * (kDwChans / kDwVec);  // 256
-constexpr int kDwBlocksPerSm = 4;  // resident blocks at <= 64 registers a thread
+constexpr int kDwBlocksPerSm = 6;  // resident blocks at <= 40 registers a thread
 
 template <typename T>
 __device__ __forceinline__ void load8(const T* src, float (&x)[kDwVec]) {
@@ -94,9 +94,11 @@ __device__ __forceinline__ void fma_w8(const float (*sWv)[kDwChans / kDwVec][4],
 // quarter tile (32 rows x 64 channels) per pass.  The gather indices of a
 // row's offsets are loaded together before its feature rows.
 //
-// Measured on B200 (406k voxels, 64 bf16 channels, L2 flushed): 129 us.
-// The kernel is bound by load latency (long-scoreboard stalls) with the L1
-// data pipe about half busy.  Variants that were slower: whole tiles per
+// Measured on B200 (406k voxels, 64 bf16 channels, L2 flushed): 123 us at
+// six resident blocks per SM (40 registers, a few bytes spilled); 129 us at
+// four (61 registers), 135 us at eight (32 registers, more spills).  The
+// kernel is bound by load latency (long-scoreboard stalls) with the L1 data
+// pipe about half busy.  Variants that were slower: whole tiles per
 // block with the indices staged in shared memory and 9 predicated loads in
 // flight per thread (223 us); the same batching in this layout (147 us);
 // staging each tile's distinct source rows in shared memory from a
