@@ -9,19 +9,24 @@
 //
 // One CTA per (256 query rows of one sequence, head), 384 threads:
 //   warp 0     TMA producer: the two 128-row Q tiles once, then per 128-key
-//              tile the K tile and the V tile into a 4-slot ring
+//              tile the K tile and the V tile into a 4-slot ring.  Q, K and
+//              V are read where they lie, [tokens, H, 64], by 3-D boxes of
+//              128 rows of one head
 //   warp 1     TMEM owner and single-thread MMA issuer over the steps
 //              i = j * groups + g (key tile j, query group g): S of step i
 //              = Q_g K_j^T goes into one of three 128-column S buffers shared
 //              by the groups (buffer i % 3); when group g's softmax has
 //              written P over the first 64 columns of that buffer, O_g +=
 //              P V_j reads P as its A operand from tensor memory and V from
-//              shared memory (MN-major), and once that product is done, S of step i + 3
-//              goes into the freed buffer.  So a group usually finds its next
-//              S computed while it still works on the current tile, and the
-//              tensor core alternates between the groups (S: M 128, N 128,
-//              K 64; PV: M 128, N 64, K 128; f32 accumulators in tensor
-//              memory)
+//              shared memory as an MN-major operand, and once that product is
+//              done, S of step i + 3 goes into the freed buffer.  So a group
+//              usually finds its next S computed while it still works on the
+//              current tile, and the tensor core alternates between the
+//              groups (S: M 128, N 128, K 64; PV: M 128, N 64, K 128; f32
+//              accumulators in tensor memory)
+//   warp 2     the last key tile of a sequence also holds rows of the next
+//              one: their weights are 0, and this warp zeroes their V rows
+//              in shared memory (0 * NaN would be NaN)
 //   warps 4-7, 8-11  softmax groups 0 and 1, one query row per thread (TMEM
 //              lane): two passes over its S row (row max, then
 //              p = 2^(s*scale*log2 e - m) and its sum), P as packed bf16/f16
@@ -31,35 +36,33 @@
 //              (conditional rescaling, the running-max trick of
 //              FlashAttention-4), and only then is the row of O rescaled
 //              in tensor memory.
-// Measured on B200 (32k tokens x 16 heads): 691-708 TFLOP/s (711 with V
-// transposed first, see below; the 10,000 + 6,384-token call gains more from
-// dropping that pass, 0.99 -> 0.958 ms).  Earlier layouts:
-// one S buffer per group, the next S issued right after the group's P was
-// written (before its P V) 625, after its P V 563; P staged in shared memory
-// in the 128B swizzle (eight 16-byte stores per 64 keys and a proxy fence
-// per tile instead of one tcgen05.st) 540; before the packed f32x2
-// arithmetic of the weight loop 532.  Computing one in eight / four of the
-// weights with a cubic 2^f polynomial on the FMA pipe instead of ex2
-// (FlashAttention-4's offload; packed f32x2, fitted to 7.5e-5 relative
-// error) measured 637 / 564 against 711 with this layout (507 / 492 against
-// 540 with the first): the softmax is bound by its instruction stream, not
-// by the ex2 unit.  64-key tiles with S double-buffered per group measured 428: the
-// fixed per-tile costs (barrier waits, fences, row-max tail) double, and an
-// N = 64 product reads more shared memory per FLOP than N = 128.  Keeping
-// keys 64..127 of S in registers from the row-max pass to the weight pass
-// (one TMEM read fewer per tile, their P at columns 64..95): 698-720, no
-// change.  Two threads per query row (eight softmax warps per group, each
-// warp on 64 of a tile's 128 keys, the half-row maxima exchanged through
-// shared memory under a named barrier per tile): 596 against 691, and the
-// 16k-token call 1.087 against 0.956 ms -- the per-tile exchange and
-// barrier cost more than the extra warps hide.
-// Q, K and V are read where they lie, [tokens, H, 64], by 3-D TMA boxes of
-// 128 rows of one head; Q and K are K-major operands, V an MN-major one.  An
-// earlier build transposed V per head into a K-major V^T first: a separate
-// 27 us pass and a buffer the size of V on the 16k-token call, and its
-// kernel ran 1-3% faster on a single 32k sequence.  Key columns past the
-// sequence end get p = 0, and warp 2 zeroes their V rows in shared memory.
 // Every mbarrier wait is bounded (SC_ETIMEOUT).
+//
+// Measured on B200, 32k tokens x 16 heads in one sequence: 691-708 TFLOP/s;
+// the 10,000 + 6,384-token call 0.958 ms.  Earlier layouts, at 32k:
+//   * V transposed per head into a K-major V^T by a separate pass first:
+//     711, the 16k-token call 0.99 ms (the pass took 27 us and a zeroed
+//     buffer the size of V);
+//   * one S buffer per group, the group's next S issued right after its P
+//     was written (before its P V) 625, after its P V 563;
+//   * P staged in shared memory in the 128B swizzle (eight 16-byte stores
+//     per 64 keys and a proxy fence per tile instead of one tcgen05.st) 540;
+//     before the packed f32x2 arithmetic of the weight loop 532.
+// Measured and dropped:
+//   * one in eight / four of the weights from a cubic 2^f polynomial on the
+//     FMA pipe instead of ex2 (FlashAttention-4's offload; packed f32x2,
+//     fitted to 7.5e-5 relative error): 637 / 564 against 711 with the S
+//     ring (507 / 492 against 540 with the first layout): the softmax is
+//     bound by its instruction stream, not by the ex2 unit;
+//   * 64-key tiles with S double-buffered per group: 428 (the fixed per-tile
+//     costs double, and an N = 64 product reads more shared memory per FLOP
+//     than N = 128);
+//   * keys 64..127 of S kept in registers from the row-max pass to the weight
+//     pass (one TMEM read fewer per tile): 698-720, no change;
+//   * two threads per query row (eight softmax warps per group, each on 64
+//     of a tile's 128 keys, half-row maxima exchanged through shared memory
+//     under a named barrier per tile): 596 against 691, the 16k-token call
+//     1.087 against 0.956 ms.
 #include "sc_common.cuh"
 #include "sc_internal.h"
 
@@ -78,7 +81,7 @@ namespace {
 constexpr int kAttnD = 64;          // head dim
 constexpr int kAttnTile = 128;      // query rows per softmax group and keys per step
 constexpr int kAttnStages = 4;      // K / V ring
-constexpr int kAttnThreads = 384;   // 12 warps: producer, MMA, 2 idle, 2 softmax groups of 4
+constexpr int kAttnThreads = 384;   // 12 warps: producer, MMA, V tail, idle, 2 softmax groups of 4
 constexpr int kTileBytes = kAttnTile * kAttnD * 2;   // 16 KB: Q, K or V tile
 // shared-memory plan (1024-byte aligned pieces)
 constexpr int kOffQ = 0;                                           // Q of group 0, group 1 at +16 KB
