@@ -39,7 +39,9 @@
 // Every mbarrier wait is bounded (SC_ETIMEOUT).
 //
 // Measured on B200, 32k tokens x 16 heads in one sequence: 691-708 TFLOP/s;
-// the 10,000 + 6,384-token call 0.958 ms.  Earlier layouts, at 32k:
+// the 10,000 + 6,384-token call 0.94-0.95 ms (0.954 with all 128 softmax
+// threads arriving on the P barrier instead of one per warp).  Earlier
+// layouts, at 32k:
 //   * V transposed per head into a K-major V^T by a separate pass first:
 //     711, the 16k-token call 0.99 ms (the pass took 27 us and a zeroed
 //     buffer the size of V);
@@ -300,7 +302,8 @@ __device__ __forceinline__ void softmax_group(const AttnParams& p, const AttnTil
     }
     tmem_wait_st();
     tc_fence_before();
-    mbar_arrive(p_full0 + 8u * b);  // P_g(j) and the O rescale (tcgen05.st) are complete
+    __syncwarp();
+    if (lane == 0) mbar_arrive(p_full0 + 8u * b);  // P_g(j) and the O rescale (tcgen05.st) are complete
     const unsigned long long s2 = add_f2(add_f2(sumv[0], sumv[1]), add_f2(sumv[2], sumv[3]));
     float sa2, sb2;
     f2_split(s2, sa2, sb2);
@@ -363,7 +366,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int sb = 0; sb < kSBufs; ++sb) {
       mbar_init(s_full0 + 8 * sb, 1);
-      mbar_init(p_full0 + 8 * sb, 128);
+      mbar_init(p_full0 + 8 * sb, 4);  // one arrival per softmax warp
     }
     mbar_init(o_done0, 1);
     mbar_init(o_done0 + 8, 1);
